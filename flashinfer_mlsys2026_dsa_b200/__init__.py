@@ -1,0 +1,11 @@
+"""B200-native DeepSeek sparse-attention (DSA) sparse-MLA decode.
+
+Drop-in for the reference solution's entry point
+``kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse)``
+(Dogacel/flashinfer-mlsys2026-dsa, solution/triton/fused.py:150), backed by one
+hand-written sm_100a CUDA kernel reached through the C ABI in include/dsa_b200.h.
+"""
+from .ops import DSAError, decode, kernel, read_device_errors, workspace_for  # noqa: F401
+
+__all__ = ["kernel", "decode", "read_device_errors", "workspace_for", "DSAError"]
+__version__ = "0.1.0"

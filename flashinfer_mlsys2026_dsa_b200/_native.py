@@ -1,0 +1,88 @@
+"""ctypes binding of the C ABI in include/dsa_b200.h (libdsa_b200.so).
+
+Loading fails loudly: there is no CPU or framework fallback for the decode.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+DSA_OK = 0
+DEVERR_BAD_INDEX = 1
+DEVERR_TIMEOUT = 2
+
+_c = ctypes
+_DECODE_ARGTYPES = [
+    _c.c_void_p, _c.c_int64, _c.c_int64,            # q_nope, stride_b, stride_h
+    _c.c_void_p, _c.c_int64, _c.c_int64,            # q_pe, stride_b, stride_h
+    _c.c_void_p, _c.c_int64,                        # ckv_cache, slot stride
+    _c.c_void_p, _c.c_int64,                        # kpe_cache, slot stride
+    _c.c_int64,                                     # num_slots
+    _c.c_void_p, _c.c_int64,                        # sparse_indices, stride_b
+    _c.c_float,                                     # sm_scale
+    _c.c_void_p, _c.c_int64, _c.c_int64,            # output, stride_b, stride_h
+    _c.c_void_p, _c.c_int64, _c.c_int64,            # lse, stride_b, stride_h
+    _c.c_int64, _c.c_int32, _c.c_int32,             # num_tokens, num_heads, topk
+    _c.c_void_p, _c.c_size_t,                       # workspace, bytes
+    _c.c_void_p,                                    # stream
+]
+
+EXPORTED_SYMBOLS = (
+    "dsa_sparse_mla_decode",
+    "dsa_sparse_mla_decode_workspace_size",
+    "dsa_read_error_word",
+    "dsa_selftest_bounded_wait",
+    "dsa_status_string",
+    "dsa_abi_version",
+)
+
+
+class NativeLibraryError(RuntimeError):
+    pass
+
+
+def library_path() -> str:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True):
+    """Load libdsa_b200.so (building it with nvcc if it is missing)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if not os.path.exists(path):
+            if not build_if_missing:
+                raise NativeLibraryError(f"{path} is missing; run flashinfer_mlsys2026_dsa_b200.build")
+            _build.build()
+        try:
+            lib = ctypes.CDLL(path)
+        except OSError as e:
+            raise NativeLibraryError(f"cannot load {path}: {e}") from e
+        lib.dsa_sparse_mla_decode.restype = _c.c_int
+        lib.dsa_sparse_mla_decode.argtypes = _DECODE_ARGTYPES
+        lib.dsa_sparse_mla_decode_workspace_size.restype = _c.c_size_t
+        lib.dsa_sparse_mla_decode_workspace_size.argtypes = [_c.c_int64, _c.c_int32, _c.c_int32,
+                                                             _c.c_int32]
+        lib.dsa_read_error_word.restype = _c.c_int
+        lib.dsa_read_error_word.argtypes = [_c.c_void_p, _c.c_void_p, _c.c_int,
+                                            _c.POINTER(_c.c_uint32)]
+        lib.dsa_selftest_bounded_wait.restype = _c.c_int
+        lib.dsa_selftest_bounded_wait.argtypes = [_c.c_int64, _c.c_void_p, _c.c_void_p]
+        lib.dsa_status_string.restype = _c.c_char_p
+        lib.dsa_status_string.argtypes = [_c.c_int]
+        lib.dsa_abi_version.restype = _c.c_int
+        lib.dsa_abi_version.argtypes = []
+        _lib = lib
+        return lib
+
+
+def status_text(code: int) -> str:
+    return load().dsa_status_string(int(code)).decode()

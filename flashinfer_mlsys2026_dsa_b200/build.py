@@ -1,0 +1,57 @@
+"""Build the native library ``libdsa_b200.so`` in-tree with nvcc for sm_100a.
+
+The library holds the CUDA kernels and the C ABI declared in
+``include/dsa_b200.h``.  It links the CUDA runtime dynamically, so inside a
+PyTorch process it shares the runtime (current device, streams) torch loaded.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+INCLUDE = os.path.join(REPO_DIR, "include")
+LIB_NAME = "libdsa_b200.so"
+LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
+SOURCES = [os.path.join(CSRC, "dsa_decode.cu")]
+DEPS = SOURCES + [os.path.join(CSRC, "sm100_ptx.cuh"), os.path.join(INCLUDE, "dsa_b200.h")]
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: the DSA decode library cannot be built")
+
+
+def is_stale() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    return any(os.path.getmtime(d) > t for d in DEPS)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not is_stale():
+        return LIB_PATH
+    tmp = LIB_PATH + f".tmp{os.getpid()}"
+    cmd = [nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+           "-Xcompiler", "-fPIC", "-shared", "-cudart", "shared",
+           "-Xlinker", "-rpath,/usr/local/cuda/lib64",
+           "-I", INCLUDE, "-I", CSRC, "-o", tmp, *SOURCES]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,163 @@
+"""Python entry points of the DSA sparse-MLA decode (PyTorch tensors in, CUDA out).
+
+``kernel`` mirrors the reference solution's destination-passing entry point
+``kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
+lse)`` (solution/triton/fused.py:150-180; same signature as
+solution/triton/baseline.py:12): same argument names, order and meaning, the
+outputs written in place, nothing returned.  ``decode`` is the value-returning
+form (``destination_passing_style: false`` in the reference README).
+
+Both call the native library through its C ABI (include/dsa_b200.h) on the
+current CUDA stream.  There is no CPU path: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _native
+
+D_CKV = 512
+D_KPE = 64
+PAGE_SIZE = 64
+SUPPORTED_HEADS = (16, 32, 64, 128)
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+class DSAError(RuntimeError):
+    """A non-zero status from the native library."""
+
+
+def _check(code: int, what: str) -> None:
+    if code != _native.DSA_OK:
+        raise DSAError(f"{what}: {_native.status_text(code)} (status {code})")
+
+
+def workspace_for(device: torch.device, stream_handle: int, num_tokens: int, num_heads: int,
+                  topk: int) -> torch.Tensor:
+    """The cached, zero-initialised workspace of (device, stream), grown on demand."""
+    lib = _native.load()
+    need = int(lib.dsa_sparse_mla_decode_workspace_size(num_tokens, num_heads, topk,
+                                                        device.index or 0))
+    if need == 0:
+        raise ValueError(f"unsupported problem: num_heads={num_heads}, topk={topk}")
+    key = (device.index or 0, stream_handle)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws
+
+
+def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
+    tensors = dict(q_nope=q_nope, q_pe=q_pe, ckv_cache=ckv_cache, kpe_cache=kpe_cache,
+                   sparse_indices=sparse_indices, output=output, lse=lse)
+    for name, t in tensors.items():
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (this operator has no CPU path)")
+    dev = q_nope.device
+    for name, t in tensors.items():
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, expected {dev}")
+    for name in ("q_nope", "q_pe", "ckv_cache", "kpe_cache", "output"):
+        if tensors[name].dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bfloat16, got {tensors[name].dtype}")
+    if sparse_indices.dtype != torch.int32:
+        raise TypeError(f"sparse_indices must be int32, got {sparse_indices.dtype}")
+    if lse.dtype != torch.float32:
+        raise TypeError(f"lse must be float32, got {lse.dtype}")
+    if q_nope.dim() != 3 or q_nope.shape[-1] != D_CKV:
+        raise ValueError(f"q_nope must be [num_tokens, num_heads, {D_CKV}], got {tuple(q_nope.shape)}")
+    B, H, _ = q_nope.shape
+    if tuple(q_pe.shape) != (B, H, D_KPE):
+        raise ValueError(f"q_pe must be [{B}, {H}, {D_KPE}], got {tuple(q_pe.shape)}")
+    if ckv_cache.shape[-1] != D_CKV or kpe_cache.shape[-1] != D_KPE:
+        raise ValueError("ckv_cache / kpe_cache last dims must be 512 / 64")
+    if sparse_indices.dim() != 2 or sparse_indices.shape[0] != B:
+        raise ValueError(f"sparse_indices must be [{B}, topk], got {tuple(sparse_indices.shape)}")
+    if tuple(output.shape) != (B, H, D_CKV):
+        raise ValueError(f"output must be [{B}, {H}, {D_CKV}], got {tuple(output.shape)}")
+    if tuple(lse.shape) != (B, H):
+        raise ValueError(f"lse must be [{B}, {H}], got {tuple(lse.shape)}")
+    if H not in SUPPORTED_HEADS:
+        raise ValueError(f"num_heads={H} is not supported (supported: {SUPPORTED_HEADS})")
+
+
+def _slot_view(cache: torch.Tensor, width: int) -> torch.Tensor:
+    """[..., page, width] cache as [num_slots, width] rows without copying when possible."""
+    if cache.stride(-1) != 1:
+        cache = cache.contiguous()
+    flat = cache.reshape(-1, width)  # a view for page-uniform strides (fused.py:155-156)
+    return flat
+
+
+def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse) -> None:
+    """DSA sparse-MLA decode, destination-passing (writes ``output`` and ``lse``).
+
+    q_nope [B,H,512] bf16, q_pe [B,H,64] bf16, ckv_cache [P,64,512] bf16,
+    kpe_cache [P,64,64] bf16, sparse_indices [B,topk] int32 flat slot ids
+    (page*64 + offset; -1 = padding), sm_scale float, output [B,H,512] bf16,
+    lse [B,H] fp32 (base-2 log-sum-exp).  Runs on the current CUDA stream
+    and does not synchronise.
+    """
+    _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
+    lib = _native.load()
+    B, H, _ = q_nope.shape
+    topk = sparse_indices.shape[1]
+    if B == 0:
+        return
+    if q_nope.stride(-1) != 1:
+        q_nope = q_nope.contiguous()
+    if q_pe.stride(-1) != 1:
+        q_pe = q_pe.contiguous()
+    if sparse_indices.stride(-1) != 1:
+        sparse_indices = sparse_indices.contiguous()
+    ckv = _slot_view(ckv_cache, D_CKV)
+    kpe = _slot_view(kpe_cache, D_KPE)
+    if ckv.shape[0] != kpe.shape[0]:
+        raise ValueError("ckv_cache and kpe_cache hold different slot counts")
+    out_t = output if output.stride(-1) == 1 else torch.empty_like(output, memory_format=torch.contiguous_format)
+    stream = torch.cuda.current_stream(q_nope.device)
+    ws = workspace_for(q_nope.device, stream.cuda_stream, B, H, topk)
+    rc = lib.dsa_sparse_mla_decode(
+        q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
+        q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
+        ckv.data_ptr(), ckv.stride(0),
+        kpe.data_ptr(), kpe.stride(0), ckv.shape[0],
+        sparse_indices.data_ptr(), sparse_indices.stride(0),
+        float(sm_scale),
+        out_t.data_ptr(), out_t.stride(0), out_t.stride(1),
+        lse.data_ptr(), lse.stride(0), lse.stride(1),
+        B, H, topk, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+    _check(rc, "dsa_sparse_mla_decode")
+    if out_t is not output:
+        output.copy_(out_t)
+
+
+def decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):
+    """Value-returning form of :func:`kernel`: returns (output, lse)."""
+    B, H, _ = q_nope.shape
+    output = torch.empty(B, H, D_CKV, dtype=torch.bfloat16, device=q_nope.device)
+    lse = torch.empty(B, H, dtype=torch.float32, device=q_nope.device)
+    kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse)
+    return output, lse
+
+
+def read_device_errors(device=None, clear: bool = True) -> int:
+    """Sticky device error bits (bad index, timeout) of the current stream's workspace."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    stream = torch.cuda.current_stream(device)
+    ws = _workspaces.get((device.index or 0, stream.cuda_stream))
+    if ws is None:
+        return 0
+    word = ctypes.c_uint32(0)
+    _check(_native.load().dsa_read_error_word(ws.data_ptr(), stream.cuda_stream, int(clear),
+                                              ctypes.byref(word)), "dsa_read_error_word")
+    return int(word.value)

@@ -1,0 +1,121 @@
+/*
+ * dsa_b200.h -- C ABI of the B200 (sm_100a) DeepSeek sparse-attention (DSA)
+ * sparse-MLA decode operator.
+ *
+ * This ABI is the native slot the reference leaves empty: the reference's CUDA
+ * solution directory holds only an empty `__global__ void kernel()` template
+ * (solution/cuda/kernel.cu:13) and an empty TVM-FFI binding registered as
+ * "flashinfer.kernel" (solution/cuda/binding.py:11-25).  The Python entry point
+ * the reference actually runs is the destination-passing
+ *     kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale,
+ *            output, lse)
+ * of solution/triton/fused.py:150-180 (same signature in
+ * solution/triton/baseline.py:12 and solution/cutedsl/kernel.py:148).
+ * dsa_sparse_mla_decode() below is that call with the tensors lowered to
+ * plain device pointers, element strides and sizes.
+ *
+ * Conventions (all functions):
+ *   - pointers are CUDA device pointers on the current device unless noted;
+ *   - strides are in ELEMENTS; the innermost dimension is contiguous;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - calls are asynchronous with respect to the host and return a status code
+ *     (DSA_OK == 0); no function traps or asserts on the device.
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+enum {
+  DSA_OK = 0,
+  DSA_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride */
+  DSA_ERR_UNSUPPORTED = 2,      /* head count / shape this build does not support */
+  DSA_ERR_MISALIGNED = 3,       /* pointer or stride violates the 16-byte TMA rule */
+  DSA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
+  DSA_ERR_CUDA = 5,             /* a CUDA runtime call or the launch failed */
+  DSA_ERR_DRIVER = 6            /* cuTensorMapEncodeTiled unavailable / rejected */
+};
+
+/* Bits of the sticky device error word kept in the workspace. */
+enum {
+  DSA_DEVERR_BAD_INDEX = 1u, /* an index < -1 or >= num_slots was seen; treated as padding */
+  DSA_DEVERR_TIMEOUT = 2u    /* a pipeline wait ran past its bound; the CTA stopped early */
+};
+
+/*
+ * Sparse-MLA decode, destination-passing style.
+ * Replaces: fused.py:150-180 `kernel(...)` (and baseline.py:12 for any head count).
+ *
+ *   q_nope     [num_tokens, num_heads, 512] bf16, strides (q_nope_stride_b, q_nope_stride_h, 1)
+ *   q_pe       [num_tokens, num_heads, 64]  bf16, strides (q_pe_stride_b,   q_pe_stride_h,   1)
+ *   ckv_cache  [num_slots, 512] bf16, row stride ckv_slot_stride  (the paged
+ *              [num_pages, 64, 512] cache viewed as slots, fused.py:155)
+ *   kpe_cache  [num_slots, 64]  bf16, row stride kpe_slot_stride  (fused.py:156)
+ *   sparse_indices [num_tokens, topk] int32, row stride indices_stride_b;
+ *              flat slot id = page * 64 + offset, -1 = padding (contributes 0)
+ *   output     [num_tokens, num_heads, 512] bf16 (written)
+ *   lse        [num_tokens, num_heads] fp32, base-2 log-sum-exp (written)
+ *   workspace  device buffer of at least dsa_sparse_mla_decode_workspace_size()
+ *              bytes, zero-filled once before its first use; the call leaves it
+ *              ready for the next call.  Calls sharing a workspace must be
+ *              ordered on one stream.
+ *
+ * num_heads must be 16, 32, 64 or 128; topk >= 1.  Base addresses and the
+ * byte value of every row stride must be multiples of 16.  A concatenated
+ * [num_slots, 576] cache is accepted by passing kpe_cache = ckv_cache + 512
+ * with both slot strides 576.  A row whose indices are all -1 gets output 0
+ * and lse -inf.
+ */
+int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h,
+                          const void* q_pe, int64_t q_pe_stride_b, int64_t q_pe_stride_h,
+                          const void* ckv_cache, int64_t ckv_slot_stride,
+                          const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots,
+                          const int32_t* sparse_indices, int64_t indices_stride_b,
+                          float sm_scale, void* output, int64_t output_stride_b,
+                          int64_t output_stride_h, float* lse, int64_t lse_stride_b,
+                          int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads,
+                          int32_t topk, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Bytes of workspace dsa_sparse_mla_decode() needs for this problem on
+ * `device` (split-K partials, per-row merge counters, the error word).
+ * Returns 0 for an unsupported shape.  No counterpart in the reference (its
+ * kernels hold no split-K state); fused.py:148 documents that it allocates
+ * nothing per call, which the caller-owned workspace preserves.
+ */
+size_t dsa_sparse_mla_decode_workspace_size(int64_t num_tokens, int32_t num_heads, int32_t topk,
+                                            int32_t device);
+
+/*
+ * Reads the sticky device error word (DSA_DEVERR_* bits) of `workspace` after
+ * synchronizing `stream`; clears it when `clear` is non-zero.  Host pointer
+ * `word` receives the value.  No counterpart in the reference (its kernels do
+ * no index checking: fused.py:89-91 only maps -1 to slot 0).
+ */
+int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word);
+
+/*
+ * Failure-detection self test: launches one CTA that waits on an mbarrier no
+ * one arrives at, bounded by `timeout_ns`, then records DSA_DEVERR_TIMEOUT in
+ * the workspace error word and returns.  Lets a test check the bounded-wait
+ * path without faulting or hanging the GPU.  No counterpart in the reference.
+ */
+int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream);
+
+/* Human-readable text of a status code (static storage). */
+const char* dsa_status_string(int status);
+
+/* ABI version: bumped when a signature above changes. */
+int dsa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */
