@@ -10,27 +10,32 @@
 // Design (B200-first, not a translation of the Triton kernel fused.py:26-144):
 //   * Work = (row, head-group, 64-slot tile) units laid out row-major; each CTA of a
 //     persistent grid (one CTA per SM) takes a contiguous, equal share of units
-//     (stream-K).  A row cut between CTAs is finished by the CTA that arrives last at
-//     the row's counter, which merges the LSE-weighted partials (split-K merge fused
-//     into the same launch).
-//   * Warp 0 (producer): per tile, reads 64 slot ids and issues TMA tile::gather4
-//     loads (4 slots x 128 B each) of the 512-d ckv row and the 64-d kpe row into a
-//     128-byte-swizzled shared-memory stage; a -1 slot is requested as an
+//     (stream-K).  A row cut between CTAs leaves one partial (unnormalised O, running
+//     max, sum) per CTA; a second small kernel merges them (LSE-weighted).  Merging
+//     inside the decode kernel would put several dependent global round trips on
+//     the tail of the merging CTA while the gathers of the others load the memory
+//     system.
+//   * Warp 0 loads each segment's Q.  Warps 1-3, 5-7, 9-11 (producers): per 64-slot
+//     tile, read the slot ids and issue 144 TMA tile::gather4 loads (4 slots x 128 B each) of the 512-d ckv rows and the
+//     64-d kpe rows into a 128-byte-swizzled shared-memory stage, the loads dealt
+//     over all nine warps (one warp issues them too slowly) and completing on one
+//     mbarrier per d-block; a -1 slot is requested as an
 //     out-of-range row, which reads nothing from HBM.  Tiles with no valid slot skip
 //     both MMAs; in other tiles the softmax warps clear a padded slot's value row so
 //     that its P == 0 contributes exactly zero.
-//   * Warp 1 (MMA issuer, one thread): score S^T[64 slots x NHC heads] = K . Q^T with
-//     tcgen05.mma (M=64, K=576 as 36 k-steps) into TMEM, then after softmax the
+//   * Warp 4 (MMA issuer, one thread): score S^T[slots x NHC heads] = K . Q^T with
+//     tcgen05.mma (M=64, K=576 as 36 k-steps, each d-block as soon as it lands) into
+//     TMEM, then after softmax the
 //     output O^T[512 d x NHC heads] += V^T . P^T (M=128 x 4 d-tiles, V read from the
 //     same stage as an MN-major operand) into TMEM.
-//   * Warps 2-5 (softmax + epilogue): tcgen05.ld the scores, base-2 online softmax
+//   * Warps 12-15 (softmax + epilogue, given most of the register file): tcgen05.ld the scores, base-2 online softmax
 //     with a lazily-updated running max (the accumulator is rescaled only when a
 //     score exceeds the running max by more than kTau), write bf16 P^T to shared
 //     memory, and at a segment's end read O from TMEM and write the output or a
 //     partial.
 //   * Heads are split into groups of NHC = min(H, 64) per unit (H = 128 -> 2 groups).
 //
-// Every mbarrier wait is bounded (wait_bounded); on timeout the CTA records
+// Every mbarrier wait is bounded (Waiter); on timeout the CTA records
 // DSA_DEVERR_TIMEOUT, stops issuing work and exits after its copies land.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -47,16 +52,26 @@ namespace dsa {
 
 constexpr int kDCkv = 512;            // latent (value) width
 constexpr int kDKpe = 64;             // rope key width
-constexpr int kBK = 64;               // slots per tile (MMA M of the score)
+constexpr int kBK = 64;               // slots per tile (the M of the score MMA)
 constexpr int kNDB = 9;               // 64-element d-blocks: 8 ckv + 1 kpe
 constexpr int kRegion = kBK * 128;    // bytes of one d-block of a stage
 constexpr int kStageBytes = kNDB * kRegion;
-constexpr int kThreads = 192;
-constexpr int kSmThreads = 128;       // softmax / epilogue warpgroup
+constexpr int kUnits = (kBK / 4) * kNDB;  // gather4 copies per tile
+constexpr int kThreads = 512;         // four warpgroups
+constexpr int kQWarp = 0;             // loads Q (one TMA box per d-block and segment)
+constexpr int kProducerWarps = 9;     // warps 1-3, 5-7 and 9-11 issue the gathers
+constexpr int kMmaWarp = 4;           // sub-partition 0 (warps 0, 4, 8, 12) issues no gathers
+constexpr int kIdleWarp = 8;
+constexpr int kSmWarp0 = 12;          // warps 12-15: softmax / epilogue
+constexpr int kSmThreads = 128;
 constexpr uint32_t kNamedBar = 1;
+constexpr uint32_t kRegsLow = 80;     // producer / MMA warpgroups after the split
+constexpr uint32_t kRegsHigh = 248;   // softmax warpgroup after the split
 constexpr float kTau = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+static_assert(kProducerWarps * 32 >= kUnits, "one gather per producer lane per tile");
+static_assert(kBK == 64, "the M=64 score tile and the 64-bit slot masks assume 64 slots");
 
 template <int NHC>
 struct Cfg {
@@ -65,13 +80,13 @@ struct Cfg {
   static constexpr int PBUF = (NHC <= 32) ? 2 : 1;
   static constexpr int Q_REGION = NHC * 128;
   static constexpr int Q_BYTES = kNDB * Q_REGION;
-  static constexpr int P_BYTES = NHC * 128;
+  static constexpr int P_BYTES = NHC * 128;  // P^T [NHC x 64] bf16
   static constexpr int OFF_KV = 0;
   static constexpr int OFF_Q = OFF_KV + STAGES * kStageBytes;
   static constexpr int OFF_P = OFF_Q + QBUF * Q_BYTES;
   static constexpr int OFF_BAR = OFF_P + PBUF * P_BYTES;
-  static constexpr int OFF_MASK = OFF_BAR + 256;
-  static constexpr int OFF_MISC = OFF_MASK + 64;
+  static constexpr int OFF_MASK = OFF_BAR + 512;
+  static constexpr int OFF_MISC = OFF_MASK + 160;
   static constexpr int OFF_RED = OFF_MISC + 64;
   static constexpr int SMEM_USED = OFF_RED + 4 * NHC * 4;
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack to 1024-align the base
@@ -84,14 +99,19 @@ struct Cfg {
                                                       : 512;
   static constexpr int SLOT_FLOATS = NHC * kDCkv + 2 * NHC;  // partial O, m, l
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(STAGES * kProducerWarps * 8 <= 160, "mask words");
   static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0, "swizzle atoms need 1024-B alignment");
 };
 
 // Barrier slots (8 bytes each) inside the OFF_BAR block.
+// Per stage: B_META (the producers' slot masks are written) and one B_KVF per d-block,
+// so that the score MMAs of d-block j can start as soon as its 8 KB have landed.
 enum : int {
-  B_KVF = 0, B_KVE = 4, B_QF = 8, B_QE = 10, B_SF = 12, B_SE = 14, B_PF = 16, B_PD = 18,
-  B_DRAIN = 20  // used only when the MMA issuer stops early
+  B_META = 0, B_KVF = 4, B_KVE = 40, B_QF = 44, B_QE = 46, B_SF = 48, B_SE = 50, B_PF = 52,
+  B_PD = 54,
+  B_DRAIN = 56  // used only when the MMA issuer stops early
 };
+__host__ __device__ constexpr int kvf(int stage, int j) { return B_KVF + stage * kNDB + j; }
 
 struct Params {
   const int32_t* idx;
@@ -107,7 +127,6 @@ struct Params {
   int32_t tpr;    // tiles per (row, head-group)
   float scale_log2;
   uint32_t* err;
-  int32_t* counters;
   float* parts;
 };
 
@@ -134,14 +153,20 @@ __device__ __forceinline__ uint32_t sw128_off(int h, int k) {
   return (uint32_t)((h >> 3) * 1024 + (h & 7) * 128 + ((((k >> 3) ^ (h & 7))) << 4) + (k & 7) * 2);
 }
 
+// Bounded mbarrier wait.  `spin` polls without letting the hardware suspend the thread
+// (for the latency-critical MMA issuer); otherwise try_wait may suspend it briefly.
 struct Waiter {
   volatile uint32_t* abort_flag;
   uint32_t* err;
+  bool spin = false;
+  __device__ __forceinline__ bool poll(uint32_t bar, uint32_t parity) const {
+    return spin ? ptx::mbar_test_wait(bar, parity) : ptx::mbar_try_wait(bar, parity);
+  }
   __device__ __forceinline__ bool operator()(uint32_t bar, uint32_t parity) const {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (poll(bar, parity)) return true;
     const uint64_t t0 = ptx::globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-      if (ptx::mbar_try_wait(bar, parity)) return true;
+      if (poll(bar, parity)) return true;
       if ((it & 63u) == 0) {
         if (*abort_flag) return false;
         if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
@@ -193,13 +218,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sgen + C::OFF_MISC);
-  uint64_t* masks = reinterpret_cast<uint64_t*>(sgen + C::OFF_MASK);
+  uint64_t* masks = reinterpret_cast<uint64_t*>(sgen + C::OFF_MASK);  // [STAGES][producer warp]
   float* red = reinterpret_cast<float*>(sgen + C::OFF_RED);
   auto bar = [&](int k) -> uint32_t { return sbase + (uint32_t)C::OFF_BAR + 8u * (uint32_t)k; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      ptx::mbar_init(bar(B_KVF + s), 1);
+      ptx::mbar_init(bar(B_META + s), kProducerWarps);
+      for (int j = 0; j < kNDB; ++j) ptx::mbar_init(bar(kvf(s, j)), 1);
       ptx::mbar_init(bar(B_KVE + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -216,13 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     misc[3] = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == kQWarp && lane == 0) {
     ptx::prefetch_tmap(&tm_ckv);
     ptx::prefetch_tmap(&tm_kpe);
     ptx::prefetch_tmap(&tm_qn);
     ptx::prefetch_tmap(&tm_qp);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     ptx::tmem_alloc(sbase + (uint32_t)C::OFF_MISC, (uint32_t)C::TMEM_COLS);
     ptx::tmem_relinquish();
   }
@@ -236,106 +262,127 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t u_hi = u_begin((int64_t)blockIdx.x + 1, p.units, G);
   const Waiter wait{misc + 2, p.err};
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+  if (warp == kQWarp) {
+    // ------------------------------------------------------------------ Q loader
+    ptx::regs_dec<kRegsLow>();
+    if (lane == 0) {
+      int seg = 0;
+      int64_t u = u_lo;
+      Segment s;
+      while (next_segment(u, u_hi, p.tpr, s)) {
+        const int64_t b = s.rh / p.hg_count;
+        const int hg = (int)(s.rh % p.hg_count);
+        const int qb = seg % C::QBUF;
+        if (!wait(bar(B_QE + qb), (uint32_t)(((seg / C::QBUF) & 1) ^ 1))) break;
+        ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)C::Q_BYTES);
+        const uint32_t qdst = sbase + (uint32_t)(C::OFF_Q + qb * C::Q_BYTES);
+        for (int jj = 0; jj < 8; ++jj)
+          ptx::tma_load_3d(qdst + (uint32_t)(jj * C::Q_REGION), &tm_qn, 64 * jj, hg * NHC, (int)b,
+                           bar(B_QF + qb));
+        ptx::tma_load_3d(qdst + (uint32_t)(8 * C::Q_REGION), &tm_qp, 0, hg * NHC, (int)b,
+                         bar(B_QF + qb));
+        ++seg;
+      }
+      // Let the last Q copy land before the CTA can exit.
+      if (seg > 0) {
+        const Waiter drain{misc + 3, p.err};
+        const int qb = (seg - 1) % C::QBUF;
+        drain(bar(B_QF + qb), (uint32_t)(((seg - 1) / C::QBUF) & 1));
+      }
+    }
+    __syncwarp();
+  } else if (warp == kIdleWarp) {
+    ptx::regs_dec<kRegsLow>();
+  } else if (warp < kSmWarp0 && warp != kMmaWarp) {
+    // ------------------------------------------------------------------ gather producers
+    // Each tile is kUnits gather4 copies (16 groups of 4 slots x 9 d-blocks), ordered
+    // d-block first and dealt round-robin over the producer warps, so that all warps
+    // issue in parallel and d-block 0 lands first.
+    ptx::regs_dec<kRegsLow>();
+    const int pw = warp - 1 - (warp >> 2);
+    const int unit = lane * kProducerWarps + pw;
+    const bool has_unit = unit < kUnits;
+    const int j = has_unit ? unit / 16 : 0;  // d-block
+    const int g = has_unit ? unit % 16 : 0;  // slots 4g .. 4g+3 of the tile
     const uint64_t policy = ptx::policy_evict_first();
-    int64_t i = 0;
-    int seg = 0;
+    // Slot ids of tile `uu` (unit index) for this lane's group; -1 past topk.
+    auto load_ids = [&](int64_t uu, int (&r)[4]) {
+      const int64_t rh = uu / p.tpr;
+      const int t = (int)(uu % p.tpr);
+      const int32_t* idx_row = p.idx + (rh / p.hg_count) * p.idx_sb;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k = t * kBK + 4 * g + q;
+        r[q] = (has_unit && k < p.topk) ? __ldg(idx_row + k) : -1;
+      }
+    };
     bool ok = true;
-    int64_t u = u_lo;
-    Segment s;
     int64_t last_issue[C::STAGES];
     for (int k = 0; k < C::STAGES; ++k) last_issue[k] = -1;
-    while (ok && next_segment(u, u_hi, p.tpr, s)) {
-      const int64_t b = s.rh / p.hg_count;
-      const int hg = (int)(s.rh % p.hg_count);
-      const int qb = seg % C::QBUF;
+    int cur[4], nxt[4];
+    if (u_lo < u_hi) load_ids(u_lo, cur);
+    for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
+      // The next tile's ids are requested before this tile waits for its stage, so
+      // their load latency overlaps the wait instead of adding to it.
+      if (uu + 1 < u_hi) load_ids(uu + 1, nxt);
+      const int stage = (int)(i % C::STAGES);
+      uint64_t vbits = 0;
+      bool bad = false;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (cur[q] < -1 || (int64_t)cur[q] >= p.num_slots) {
+          bad = true;
+          cur[q] = -1;
+        }
+        vbits |= (uint64_t)(cur[q] >= 0 ? 1u : 0u) << (4 * g + q);
+      }
+      if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
+      const uint64_t wmask =
+          ((uint64_t)__reduce_or_sync(0xffffffffu, (uint32_t)(vbits >> 32)) << 32) |
+          __reduce_or_sync(0xffffffffu, (uint32_t)vbits);
       if (lane == 0) {
-        ok = wait(bar(B_QE + qb), (uint32_t)(((seg / C::QBUF) & 1) ^ 1));
+        ok = wait(bar(B_KVE + stage), (uint32_t)(((i / C::STAGES) & 1) ^ 1));
         if (ok) {
-          ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)C::Q_BYTES);
-          const uint32_t qdst = sbase + (uint32_t)(C::OFF_Q + qb * C::Q_BYTES);
-          for (int j = 0; j < 8; ++j)
-            ptx::tma_load_3d(qdst + (uint32_t)(j * C::Q_REGION), &tm_qn, 64 * j, hg * NHC, (int)b,
-                             bar(B_QF + qb));
-          ptx::tma_load_3d(qdst + (uint32_t)(8 * C::Q_REGION), &tm_qp, 0, hg * NHC, (int)b,
-                           bar(B_QF + qb));
+          masks[stage * kProducerWarps + pw] = wmask;
+          ptx::mbar_arrive(bar(B_META + stage));
+          if (pw == 0)
+            for (int jj = 0; jj < kNDB; ++jj)
+              ptx::mbar_arrive_expect_tx(bar(kvf(stage, jj)), 16u * 512u);
         }
       }
       ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
       if (!ok) break;
-      const int32_t* idx_row = p.idx + b * p.idx_sb;
-      for (int t = s.t0; t < s.t1; ++t, ++i) {
-        const int stage = (int)(i % C::STAGES);
-        const int kbase = t * kBK + 4 * (lane >> 1);
-        int r[4];
-        bool bad = false;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int k = kbase + q;
-          int v = -1;
-          if (k < p.topk) {
-            v = __ldg(idx_row + k);
-            if (v < -1 || (int64_t)v >= p.num_slots) {
-              bad = true;
-              v = -1;
-            }
-          }
-          r[q] = v;
-        }
-        if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
-        uint32_t bq[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) bq[q] = __ballot_sync(0xffffffffu, r[q] >= 0);
-        if (lane == 0) {
-          ok = wait(bar(B_KVE + stage), (uint32_t)(((i / C::STAGES) & 1) ^ 1));
-          if (ok) {
-            uint64_t mask = 0;
-#pragma unroll
-            for (int g = 0; g < 16; ++g)
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                mask |= (uint64_t)((bq[q] >> (2 * g)) & 1u) << (4 * g + q);
-            masks[stage] = mask;
-            ptx::mbar_arrive_expect_tx(bar(B_KVF + stage), (uint32_t)kStageBytes);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
-        if (!ok) break;
-        last_issue[stage] = i;
-        const int4 rows = make_int4(r[0], r[1], r[2], r[3]);
-        const uint32_t dst0 =
-            sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes + (lane >> 1) * 512);
-        const int jlo = (lane & 1) ? 5 : 0;
-        const int jhi = (lane & 1) ? 9 : 5;
-        for (int j = jlo; j < jhi; ++j) {
-          if (j < 8)
-            ptx::tma_gather4(dst0 + (uint32_t)(j * kRegion), &tm_ckv, 64 * j, rows,
-                             bar(B_KVF + stage), policy);
-          else
-            ptx::tma_gather4(dst0 + (uint32_t)(j * kRegion), &tm_kpe, 0, rows, bar(B_KVF + stage),
-                             policy);
-        }
+      last_issue[stage] = i;
+      if (has_unit) {
+        const uint32_t dst = sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes + j * kRegion + g * 512);
+        const int4 rows = make_int4(cur[0], cur[1], cur[2], cur[3]);
+        if (j < 8)
+          ptx::tma_gather4(dst, &tm_ckv, 64 * j, rows, bar(kvf(stage, j)), policy);
+        else
+          ptx::tma_gather4(dst, &tm_kpe, 0, rows, bar(kvf(stage, j)), policy);
       }
-      ++seg;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
     }
     if (!ok && lane == 0) {
       // Stop early: let every copy this warp issued land before the CTA exits.
       const Waiter drain{misc + 3, p.err};
       for (int k = 0; k < C::STAGES; ++k)
-        if (last_issue[k] >= 0) drain(bar(B_KVF + k), (uint32_t)((last_issue[k] / C::STAGES) & 1));
+        if (last_issue[k] >= 0)
+          for (int jj = 0; jj < kNDB; ++jj)
+            drain(bar(kvf(k, jj)), (uint32_t)((last_issue[k] / C::STAGES) & 1));
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
+    ptx::regs_dec<kRegsLow>();
     if (lane == 0) {
+      const Waiter wait{misc + 2, p.err, true};
       constexpr uint32_t kIdescS = idesc_bf16(64, NHC, false);
       constexpr uint32_t kIdescPV = idesc_bf16(128, NHC, true);
       int64_t i = 0;
       int seg = 0;
       bool ok = true;
-      int64_t prev_i = -1;
-      bool prev_first = false, prev_live = false;
       int64_t u = u_lo;
       Segment s;
       bool o_init = false;  // O holds this segment's sum (a live tile's PV was issued)
@@ -350,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
+            for (int ks = 0; ks < kBK / 16; ++ks)
               ptx::umma_bf16(tmem + (uint32_t)(C::O_COL + mt * NHC),
                              sdesc(kv + (uint32_t)(2 * mt * kRegion + ks * 2048), kRegion, 1024),
                              sdesc(pb + (uint32_t)(ks * 32), 16, 1024), kIdescPV,
@@ -367,36 +414,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = s.t0; t < s.t1; ++t, ++i) {
           const int stage = (int)(i % C::STAGES);
           const int sb = (int)(i & 1);
+          const uint32_t kpar = (uint32_t)((i / C::STAGES) & 1);
           if (t == s.t0) ok = wait(bar(B_QF + qb), (uint32_t)((seg / C::QBUF) & 1));
-          ok = ok && wait(bar(B_KVF + stage), (uint32_t)((i / C::STAGES) & 1));
+          ok = ok && wait(bar(B_META + stage), kpar);
           ok = ok && wait(bar(B_SE + sb), (uint32_t)(((i >> 1) & 1) ^ 1));
           if (!ok) break;
-          ptx::tc_fence_after();
-          const bool live = masks[stage] != 0ull;
-          if (live) {  // an all-padding tile's scores are all masked: skip its MMAs
-            const uint32_t kv = sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes);
-            const uint32_t d_s = tmem + (uint32_t)(C::S_COL + sb * NHC);
+          uint64_t m = 0;
 #pragma unroll
-            for (int j = 0; j < kNDB; ++j)
+          for (int w = 0; w < kProducerWarps; ++w) m |= masks[stage * kProducerWarps + w];
+          const bool live = m != 0ull;
+          // S^T[64 x NHC] = K[64 x 576] . Q[NHC x 576]^T, d-block by d-block as they land.
+          // An all-padding tile's scores are all masked: its MMAs are skipped, but its
+          // copies are still waited for before the stage is handed back.
+          const uint32_t kv = sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes);
+          const uint32_t d_s = tmem + (uint32_t)(C::S_COL + sb * NHC);
+#pragma unroll 1
+          for (int jj = 0; jj < kNDB && ok; ++jj) {
+            ok = wait(bar(kvf(stage, jj)), kpar);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            if (live) {
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
-                ptx::umma_bf16(d_s, sdesc(kv + (uint32_t)(j * kRegion + ks * 32), 16, 1024),
-                               sdesc(qbase + (uint32_t)(j * C::Q_REGION + ks * 32), 16, 1024),
-                               kIdescS, (j | ks) ? 1u : 0u);
+                ptx::umma_bf16(d_s, sdesc(kv + (uint32_t)(jj * kRegion + ks * 32), 16, 1024),
+                               sdesc(qbase + (uint32_t)(jj * C::Q_REGION + ks * 32), 16, 1024),
+                               kIdescS, (jj | ks) ? 1u : 0u);
+            }
           }
+          if (!ok) break;
           ptx::umma_commit(bar(B_SF + sb));
           if (t == s.t1 - 1) ptx::umma_commit(bar(B_QE + qb));
-          if (prev_i >= 0) {
-            ok = issue_pv(prev_i, prev_first, prev_live);
-            if (!ok) break;
-          }
-          prev_i = i;
-          prev_first = (t == s.t0);
-          prev_live = live;
+          // PV(i) right behind score(i): with two stages, releasing a stage early
+          // keeps more gathers in flight than overlapping score(i+1) with softmax(i).
+          ok = issue_pv(i, t == s.t0, live);
+          if (!ok) break;
         }
         ++seg;
       }
-      if (ok && prev_i >= 0) ok = issue_pv(prev_i, prev_first, prev_live);
       if (!ok) {
         // Stop early: wait (bounded) until every MMA issued so far has retired.
         const Waiter drain{misc + 3, p.err};
@@ -407,10 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax / epilogue
+    ptx::regs_inc<kRegsHigh>();
     const int sp = warp & 3;                 // TMEM sub-partition of this warp
-    const int tid = threadIdx.x - 64;        // 0..127
+    const int tid = threadIdx.x - kSmWarp0 * 32;  // 0..127
     const uint32_t lane_base = (uint32_t)(32 * sp) << 16;
-    const int kv_row = 16 * sp + lane;       // score row (slot within the tile) of this lane
+    // Score row (slot within the tile) of this lane: the M=64 accumulator keeps
+    // rows 16*sp .. 16*sp+15 in lanes 0-15 of sub-partition sp.
+    const int kv_row = 16 * sp + lane;
+    const bool row_lane = (lane < 16) && (kv_row < kBK);
     int64_t i = 0;
     bool aborted = false;
     int64_t u = u_lo;
@@ -427,13 +485,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = s.t0; t < s.t1; ++t, ++i) {
         const int stage = (int)(i % C::STAGES);
         const int sb = (int)(i & 1);
-        const bool ok = !aborted && wait(bar(B_KVF + stage), (uint32_t)((i / C::STAGES) & 1)) &&
+        const bool ok = !aborted && wait(bar(B_META + stage), (uint32_t)((i / C::STAGES) & 1)) &&
                         wait(bar(B_SF + sb), (uint32_t)((i >> 1) & 1));
-        if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !ok)) {
-          aborted = true;
-          break;
-        }
-        const uint64_t vmask = masks[stage];
+        uint64_t vmask = 0;
+#pragma unroll
+        for (int w = 0; w < kProducerWarps; ++w) vmask |= masks[stage * kProducerWarps + w];
         ptx::tc_fence_after();
         uint32_t sr[NHC];
 #pragma unroll
@@ -442,11 +498,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tmem_ld16(tmem + lane_base + (uint32_t)(C::S_COL + sb * NHC + 16 * c), chunk);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) sr[16 * c + j] = chunk[j];
+          for (int jj = 0; jj < 16; ++jj) sr[16 * c + jj] = chunk[jj];
         }
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(B_SE + sb));
-        const bool rv = (lane < 16) && ((vmask >> kv_row) & 1ull);
+        if (ok) ptx::mbar_arrive(bar(B_SE + sb));
+        const bool rv = row_lane && ((vmask >> kv_row) & 1ull);
         float x[NHC];
         bool need = false;
 #pragma unroll
@@ -454,7 +510,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[h] = rv ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
           need |= x[h] > m_run[h] + kTau;
         }
-        if (ptx::bar_red_or(kNamedBar, kSmThreads, need)) {
+        // One vote per tile: "some score needs a new running max, or a wait failed".
+        // The rare second vote tells the two apart, so every thread agrees on both.
+        bool rescale = false;
+        if (ptx::bar_red_or(kNamedBar, kSmThreads, need || aborted || !ok)) {
+          if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !ok)) {
+            aborted = true;
+            break;
+          }
+          rescale = true;
+        }
+        if (rescale) {
 #pragma unroll
           for (int h = 0; h < NHC; ++h) {
             float v = x[h];
@@ -482,13 +548,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < NHC / 16; ++c) {
                   const uint32_t ta = tmem + lane_base + (uint32_t)(C::O_COL + mt * NHC + 16 * c);
-                  uint32_t r[16];
-                  ptx::tmem_ld16(ta, r);
+                  uint32_t rr[16];
+                  ptx::tmem_ld16(ta, rr);
                   ptx::tmem_wait_ld();
 #pragma unroll
-                  for (int j = 0; j < 16; ++j)
-                    r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha[16 * c + j]);
-                  ptx::tmem_st16(ta, r);
+                  for (int jj = 0; jj < 16; ++jj)
+                    rr[jj] = __float_as_uint(__uint_as_float(rr[jj]) * alpha[16 * c + jj]);
+                  ptx::tmem_st16(ta, rr);
                 }
               ptx::tmem_wait_st();
             }
@@ -507,18 +573,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
           const float pv = ptx::ex2(x[h] - me);
           l_part[h] += pv;
-          if (lane < 16)
+          if (row_lane)
             *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(h, kv_row)) = __float2bfloat16_rn(pv);
         }
-        if (vmask != 0ull && lane < 16 && !rv) {
+        if (vmask != 0ull && row_lane && !rv) {
           // A padded slot of a live tile: its P is 0, but 0 * (non-finite stale bytes)
           // would poison the PV sum, so clear its value row (the 8 ckv d-blocks).
           uint8_t* row = sgen + C::OFF_KV + stage * kStageBytes + kv_row * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
+          for (int jj = 0; jj < 8; ++jj)
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4*>(row + j * kRegion + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+              *reinterpret_cast<uint4*>(row + jj * kRegion + q * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
         ptx::fence_proxy_async_smem();
         ptx::tc_fence_before();
@@ -554,13 +620,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = 128 * mt + 32 * sp + lane;
 #pragma unroll
         for (int c = 0; c < NHC / 16; ++c) {
-          uint32_t r[16];
-          ptx::tmem_ld16(tmem + lane_base + (uint32_t)(C::O_COL + mt * NHC + 16 * c), r);
+          uint32_t rr[16];
+          ptx::tmem_ld16(tmem + lane_base + (uint32_t)(C::O_COL + mt * NHC + 16 * c), rr);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int h = 16 * c + j;
-            const float o = __uint_as_float(r[j]);
+          for (int jj = 0; jj < 16; ++jj) {
+            const int h = 16 * c + jj;
+            const float o = __uint_as_float(rr[jj]);
             if (full) {
               const float y = L[h] > 0.f ? o / L[h] : 0.f;
               p.out[b * p.out_sb + (int64_t)(head0 + h) * p.out_sh + d] = __float2bfloat16_rn(y);
@@ -581,85 +647,76 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       ptx::tc_fence_before();
-      if (!full) {
-        // Split row: publish the partial; the last CTA to arrive merges all of them.
-        __threadfence();
-        ptx::bar_sync(kNamedBar, kSmThreads);
-        if (tid == 0) {
-          const int64_t c_lo = cta_of(s.rh * p.tpr, p.units, G);
-          const int64_t c_hi = cta_of((s.rh + 1) * p.tpr - 1, p.units, G);
-          const int old = atomicAdd(p.counters + s.rh, 1);
-          misc[1] = (old == (int)(c_hi - c_lo)) ? 1u : 0u;
-        }
-        ptx::bar_sync(kNamedBar, kSmThreads);
-        const bool merge = misc[1] != 0;
-        if (merge) {
-          __threadfence();
-          const int64_t c_lo = cta_of(s.rh * p.tpr, p.units, G);
-          const int64_t c_hi = cta_of((s.rh + 1) * p.tpr - 1, p.units, G);
-          float M[NHC], Lt[NHC];
-#pragma unroll
-          for (int h = 0; h < NHC; ++h) {
-            M[h] = -INFINITY;
-            Lt[h] = 0.f;
-          }
-          for (int64_t c = c_lo; c <= c_hi; ++c) {
-            const int64_t sl = 2 * c + ((u_begin(c, p.units, G) / p.tpr) == s.rh ? 0 : 1);
-            const float* pp = p.parts + sl * C::SLOT_FLOATS + NHC * kDCkv;
-#pragma unroll
-            for (int h = 0; h < NHC; ++h)
-              if (__ldcg(pp + NHC + h) > 0.f) M[h] = fmaxf(M[h], __ldcg(pp + h));
-          }
-          for (int64_t c = c_lo; c <= c_hi; ++c) {
-            const int64_t sl = 2 * c + ((u_begin(c, p.units, G) / p.tpr) == s.rh ? 0 : 1);
-            const float* pp = p.parts + sl * C::SLOT_FLOATS + NHC * kDCkv;
-#pragma unroll
-            for (int h = 0; h < NHC; ++h) {
-              const float lp = __ldcg(pp + NHC + h);
-              if (lp > 0.f) Lt[h] += ptx::ex2(__ldcg(pp + h) - M[h]) * lp;
-            }
-          }
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            const int d = 128 * mt + 32 * sp + lane;
-            float acc[NHC];
-#pragma unroll
-            for (int h = 0; h < NHC; ++h) acc[h] = 0.f;
-            for (int64_t c = c_lo; c <= c_hi; ++c) {
-              const int64_t sl = 2 * c + ((u_begin(c, p.units, G) / p.tpr) == s.rh ? 0 : 1);
-              const float* pp = p.parts + sl * C::SLOT_FLOATS;
-#pragma unroll
-              for (int h = 0; h < NHC; ++h) {
-                const float lp = __ldcg(pp + NHC * kDCkv + NHC + h);
-                if (lp > 0.f) {
-                  const float w = ptx::ex2(__ldcg(pp + NHC * kDCkv + h) - M[h]);
-                  acc[h] += w * __ldcg(pp + h * kDCkv + d);
-                }
-              }
-            }
-#pragma unroll
-            for (int h = 0; h < NHC; ++h) {
-              const float y = Lt[h] > 0.f ? acc[h] / Lt[h] : 0.f;
-              p.out[b * p.out_sb + (int64_t)(head0 + h) * p.out_sh + d] = __float2bfloat16_rn(y);
-            }
-          }
-          if (tid < NHC) {
-            const int h = tid;
-            p.lse[b * p.lse_sb + (int64_t)(head0 + h) * p.lse_sh] =
-                Lt[h] > 0.f ? M[h] + ptx::lg2(Lt[h]) : -INFINITY;
-          }
-          if (tid == 0) p.counters[s.rh] = 0;
-        }
-      }
     }
   }
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, (uint32_t)C::TMEM_COLS);
   }
+}
+
+
+// Split-K merge.  CTA x of this grid looks at the boundary between decode CTAs x and x+1;
+// if that boundary cuts a (row, head-group) and it is the first boundary that does, this
+// CTA combines the row's partials (LSE-weighted, running max) for 16 heads (blockIdx.y).
+// Rows that one decode CTA finished were written directly and are not touched here.
+template <int NHC>
+__global__ void __launch_bounds__(kDCkv) dsa_merge_kernel(const __grid_constant__ Params p,
+                                                          int grid_main) {
+  using C = Cfg<NHC>;
+  const int64_t G = grid_main;
+  const int64_t c = (int64_t)blockIdx.x + 1;
+  if (c >= G) return;
+  const int64_t ub = u_begin(c, p.units, G);
+  if (ub % p.tpr == 0) return;
+  const int64_t rh = ub / p.tpr;
+  const int64_t c_lo = cta_of(rh * p.tpr, p.units, G);
+  if (c_lo != c - 1) return;
+  const int64_t c_hi = cta_of((rh + 1) * p.tpr - 1, p.units, G);
+  const int h0 = 16 * (int)blockIdx.y;
+  const int d = threadIdx.x;
+  float M[16], Lt[16], acc[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) {
+    M[h] = -INFINITY;
+    Lt[h] = 0.f;
+    acc[h] = 0.f;
+  }
+  for (int64_t cc = c_lo; cc <= c_hi; ++cc) {
+    const int64_t sl = 2 * cc + ((u_begin(cc, p.units, G) / p.tpr) == rh ? 0 : 1);
+    const float* pp = p.parts + sl * C::SLOT_FLOATS;
+    float pm[16], pl[16], po[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      pm[h] = __ldg(pp + NHC * kDCkv + h0 + h);
+      pl[h] = __ldg(pp + NHC * kDCkv + NHC + h0 + h);
+      po[h] = __ldg(pp + (h0 + h) * kDCkv + d);
+    }
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      // A part with l == 0 saw only padding; its O is never read (it may be stale).
+      const bool live = pl[h] > 0.f;
+      const float mn = live ? fmaxf(M[h], pm[h]) : M[h];
+      const float keep = (M[h] == -INFINITY) ? 0.f : ptx::ex2(M[h] - mn);
+      const float w = live ? ptx::ex2(pm[h] - mn) : 0.f;
+      Lt[h] = Lt[h] * keep + (live ? w * pl[h] : 0.f);
+      acc[h] = acc[h] * keep + (live ? w * po[h] : 0.f);
+      M[h] = mn;
+    }
+  }
+  const int64_t b = rh / p.hg_count;
+  const int head0 = (int)(rh % p.hg_count) * NHC + h0;
+#pragma unroll
+  for (int h = 0; h < 16; ++h) {
+    const float y = Lt[h] > 0.f ? acc[h] / Lt[h] : 0.f;
+    p.out[b * p.out_sb + (int64_t)(head0 + h) * p.out_sh + d] = __float2bfloat16_rn(y);
+  }
+  if (d < 16)
+    p.lse[b * p.lse_sb + (int64_t)(head0 + d) * p.lse_sh] =
+        Lt[d] > 0.f ? M[d] + ptx::lg2(Lt[d]) : -INFINITY;
 }
 
 __global__ void selftest_wait_kernel(uint32_t* err, int64_t timeout_ns) {
@@ -735,19 +792,20 @@ int nhc_for(int heads) {
   }
 }
 
-int slot_floats(int nhc) { return nhc * kDCkv + 2 * nhc; }
-
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Workspace layout, fixed for a device so that calls of any shape can share it:
+//   [0, 256)            header (word 0: sticky device error bits)
+//   [256, 256 + parts)  split-K partials: 2 slots per decode CTA, each sized for the
+//                       widest head group (64 heads) whatever this call's group width
 struct WsLayout {
-  size_t counters_off, parts_off, total;
+  size_t parts_off, total;
 };
 
-WsLayout ws_layout(int64_t num_rh, int64_t grid, int nhc) {
+WsLayout ws_layout(int sms) {
   WsLayout w;
-  w.counters_off = 256;
-  w.parts_off = align_up(w.counters_off + (size_t)num_rh * 4, 256);
-  w.total = w.parts_off + (size_t)(2 * grid) * (size_t)slot_floats(nhc) * 4;
+  w.parts_off = 256;
+  w.total = align_up(w.parts_off + (size_t)(2 * sms) * (size_t)Cfg<64>::SLOT_FLOATS * 4, 256);
   return w;
 }
 
@@ -773,6 +831,12 @@ int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_dev[dev].attr_done[ai]) {
+      // The kernel re-splits its register pool per warpgroup (setmaxnreg); refuse to
+      // launch a build whose pool is too small for that split, which would stall.
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, dsa_decode_kernel<NHC>) != cudaSuccess) return DSA_ERR_CUDA;
+      if ((int64_t)fa.numRegs * kThreads < 128 * (int64_t)(3 * kRegsLow + kRegsHigh))
+        return DSA_ERR_CUDA;
       if (cudaFuncSetAttribute(dsa_decode_kernel<NHC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                C::SMEM_BYTES) != cudaSuccess)
         return DSA_ERR_CUDA;
@@ -780,6 +844,7 @@ int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn
     }
   }
   dsa_decode_kernel<NHC><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ckv, kpe, qn, qp, prm);
+  if (grid > 1) dsa_merge_kernel<NHC><<<dim3(grid - 1, NHC / 16), kDCkv, 0, stream>>>(prm, grid);
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }
 
@@ -811,11 +876,7 @@ size_t dsa_sparse_mla_decode_workspace_size(int64_t num_tokens, int32_t num_head
   if (nhc == 0 || num_tokens < 0 || topk < 1) return 0;
   const int sms = device_sms(device);
   if (sms <= 0) return 0;
-  const int64_t num_rh = num_tokens * (num_heads / nhc);
-  const int64_t tpr = (topk + kBK - 1) / kBK;
-  const int64_t units = num_rh * tpr;
-  const int64_t grid = units < sms ? units : sms;
-  return ws_layout(num_rh, grid > 0 ? grid : 1, nhc).total;
+  return ws_layout(sms).total;
 }
 
 int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h,
@@ -853,7 +914,7 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
   const int tpr = (topk + kBK - 1) / kBK;
   const int64_t units = num_rh * tpr;
   const int64_t grid = units < sms ? units : sms;
-  const WsLayout wl = ws_layout(num_rh, grid, nhc);
+  const WsLayout wl = ws_layout(sms);
   if (!workspace || workspace_bytes < wl.total) return DSA_ERR_WORKSPACE;
 
   CUtensorMap m_ckv, m_kpe, m_qn, m_qp;
@@ -900,7 +961,6 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
   prm.tpr = tpr;
   prm.scale_log2 = sm_scale * kLog2e;
   prm.err = reinterpret_cast<uint32_t*>(ws);
-  prm.counters = reinterpret_cast<int32_t*>(ws + wl.counters_off);
   prm.parts = reinterpret_cast<float*>(ws + wl.parts_off);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);

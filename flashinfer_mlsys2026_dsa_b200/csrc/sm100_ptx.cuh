@@ -1,7 +1,7 @@
 // Thin inline-PTX wrappers for the sm_100a features the DSA decode kernel uses:
 // mbarriers, TMA tile / gather4 loads, tcgen05 (TMEM alloc, UMMA, ld/st,
-// commit, fences) and named barriers.  Every wait here is bounded by the
-// caller (see wait_bounded in dsa_decode.cu); nothing in this file spins.
+// commit, fences), register reconfiguration and named barriers.  Nothing in this
+// file spins: mbar_try_wait polls once and the callers bound their loops.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -39,6 +39,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of the same condition (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -58,7 +70,8 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
 }
 // Four rows (row coordinates r.x..r.w) of `box[0]` elements starting at column
 // `col` land as four consecutive 128-byte rows at `dst` (swizzle applied by the
-// tensor map).  Rows outside [0, dim1) are filled with zeros and read nothing.
+// tensor map).  A row coordinate outside [0, dim1) reads nothing from global
+// memory; callers must not rely on the bytes that land for such a row.
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* m, int32_t col,
                                             int4 r, uint32_t bar, uint64_t policy) {
   asm volatile(
@@ -139,6 +152,19 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- register split
+// Every warp of a warpgroup executes these.  The block's register pool is fixed at
+// launch (threads x registers per thread); the host checks that the per-warpgroup
+// targets fit in it before it launches a kernel that uses them.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------- named barriers

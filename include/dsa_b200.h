@@ -62,9 +62,9 @@ enum {
  *   output     [num_tokens, num_heads, 512] bf16 (written)
  *   lse        [num_tokens, num_heads] fp32, base-2 log-sum-exp (written)
  *   workspace  device buffer of at least dsa_sparse_mla_decode_workspace_size()
- *              bytes, zero-filled once before its first use; the call leaves it
- *              ready for the next call.  Calls sharing a workspace must be
- *              ordered on one stream.
+ *              bytes (split-K partials and the error word); zero-fill it once
+ *              before first use so that the error word starts clear.  Calls
+ *              sharing a workspace must be ordered on one stream.
  *
  * num_heads must be 16, 32, 64 or 128; topk >= 1.  Base addresses and the
  * byte value of every row stride must be multiples of 16.  A concatenated
@@ -84,7 +84,8 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
 
 /*
  * Bytes of workspace dsa_sparse_mla_decode() needs for this problem on
- * `device` (split-K partials, per-row merge counters, the error word).
+ * `device` (split-K partials and the error word; the size depends only on
+ * the device's SM count, so one workspace serves every shape).
  * Returns 0 for an unsupported shape.  No counterpart in the reference (its
  * kernels hold no split-K state); fused.py:148 documents that it allocates
  * nothing per call, which the caller-owned workspace preserves.

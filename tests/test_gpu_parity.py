@@ -207,3 +207,20 @@ def test_bounded_wait_reports_timeout_without_hanging():
     out, lse = run(to_dev(c))
     assert_close(out, lse, oracle.bf16_bits_to_f32(GOLDEN["tiny_b2_h16_k256.out"]),
                  GOLDEN["tiny_b2_h16_k256.lse"])
+
+
+def test_shared_workspace_across_batch_sizes():
+    """Calls of different batch sizes share one workspace; each must start from clean counters."""
+    w = workloads.make("b64_h16", device="cuda", seed=7, batch=256)
+    sizes = [64, 256, 128, 160, 20, 256]
+    refs = {}
+    for b in sizes:
+        args = (w.q_nope[:b].contiguous(), w.q_pe[:b].contiguous(), w.ckv_cache, w.kpe_cache,
+                w.sparse_indices[:b].contiguous(), w.sm_scale)
+        out, lse = run(args)
+        assert np.isfinite(out).all() and np.isfinite(lse).all(), f"batch {b}"
+        if b in refs:  # same shape again: bit-identical
+            np.testing.assert_array_equal(out, refs[b][0])
+        refs.setdefault(b, (out, lse))
+    ref_out, ref_lse = oracle_on_workload(w, rows=slice(0, 20))
+    assert_close(refs[20][0], refs[20][1], ref_out, ref_lse)
