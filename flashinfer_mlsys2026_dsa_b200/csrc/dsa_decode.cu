@@ -52,11 +52,16 @@ namespace dsa {
 
 constexpr int kDCkv = 512;            // latent (value) width
 constexpr int kDKpe = 64;             // rope key width
-constexpr int kBK = 64;               // slots per tile (the M of the score MMA)
+constexpr int kBK = 56;               // slots per tile (the score MMA is M=64; its last 8
+                                      // rows read the next 1 KB and are never used)
+constexpr int kMRows = 64;            // M of the score MMA = rows of P per tile
+constexpr int kGroups = kBK / 4;      // gather4 groups per d-block
 constexpr int kNDB = 9;               // 64-element d-blocks: 8 ckv + 1 kpe
 constexpr int kRegion = kBK * 128;    // bytes of one d-block of a stage
 constexpr int kStageBytes = kNDB * kRegion;
-constexpr int kUnits = (kBK / 4) * kNDB;  // gather4 copies per tile
+constexpr int kUnits = kGroups * kNDB;    // gather4 copies per tile
+constexpr int kPVSteps = kMRows / 16;     // K steps of the PV MMA (rows >= kBK carry P == 0)
+constexpr int kPVSplit = 5;               // d-block of score(i) before which PV(i-1) is issued
 constexpr int kThreads = 512;         // four warpgroups
 constexpr int kQWarp = 0;             // loads Q (one TMA box per d-block and segment)
 constexpr int kProducerWarps = 9;     // warps 1-3, 5-7 and 9-11 issue the gathers
@@ -71,13 +76,17 @@ constexpr float kTau = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 static_assert(kProducerWarps * 32 >= kUnits, "one gather per producer lane per tile");
-static_assert(kBK == 64, "the M=64 score tile and the 64-bit slot masks assume 64 slots");
+static_assert(kBK % 8 == 0 && kBK <= 64, "tile rows: whole 8-row swizzle atoms, 64-bit masks");
 
 template <int NHC>
 struct Cfg {
-  static constexpr int STAGES = 2;
-  static constexpr int QBUF = (NHC <= 32) ? 2 : 1;
-  static constexpr int PBUF = (NHC <= 32) ? 2 : 1;
+  static constexpr int STAGES = (NHC == 16) ? 3 : 2;
+  static constexpr int QBUF = (NHC == 32) ? 2 : 1;
+  static constexpr int PBUF = 2;
+  // With three stages the MMA issuer runs score(i+1) before PV(i) so that the tensor
+  // core is not idle during softmax(i); with two, PV(i) follows score(i) at once so that
+  // each stage is handed back as early as possible.
+  static constexpr bool OVERLAP = STAGES >= 3;
   static constexpr int Q_REGION = NHC * 128;
   static constexpr int Q_BYTES = kNDB * Q_REGION;
   static constexpr int P_BYTES = NHC * 128;  // P^T [NHC x 64] bf16
@@ -86,7 +95,7 @@ struct Cfg {
   static constexpr int OFF_P = OFF_Q + QBUF * Q_BYTES;
   static constexpr int OFF_BAR = OFF_P + PBUF * P_BYTES;
   static constexpr int OFF_MASK = OFF_BAR + 512;
-  static constexpr int OFF_MISC = OFF_MASK + 160;
+  static constexpr int OFF_MISC = OFF_MASK + 256;
   static constexpr int OFF_RED = OFF_MISC + 64;
   static constexpr int SMEM_USED = OFF_RED + 4 * NHC * 4;
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack to 1024-align the base
@@ -99,7 +108,7 @@ struct Cfg {
                                                       : 512;
   static constexpr int SLOT_FLOATS = NHC * kDCkv + 2 * NHC;  // partial O, m, l
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-  static_assert(STAGES * kProducerWarps * 8 <= 160, "mask words");
+  static_assert(STAGES * kProducerWarps * 8 <= 256, "mask words");
   static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0, "swizzle atoms need 1024-B alignment");
 };
 
@@ -188,6 +197,19 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t G) {
   return ((u + 1) * G - 1) / units;
 }
 
+// Slot ids of tile `uu` (unit index) for a producer lane's group g; -1 past topk.
+__device__ __forceinline__ void load_slot_ids(const Params& p, int64_t uu, bool has_unit, int g,
+                                              int (&r)[4]) {
+  const int64_t rh = uu / p.tpr;
+  const int t = (int)(uu % p.tpr);
+  const int32_t* idx_row = p.idx + (rh / p.hg_count) * p.idx_sb;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int k = t * kBK + 4 * g + q;
+    r[q] = (has_unit && k < p.topk) ? __ldg(idx_row + k) : -1;
+  }
+}
+
 struct Segment {
   int64_t rh;  // row * hg_count + head-group
   int t0, t1;  // tile range [t0, t1) within the row
@@ -200,6 +222,37 @@ __device__ __forceinline__ bool next_segment(int64_t& u, int64_t u1, int tpr, Se
   const int64_t room = u1 - u;
   s.t1 = (int)((int64_t)s.t0 + room < (int64_t)tpr ? (int64_t)s.t0 + room : (int64_t)tpr);
   u += s.t1 - s.t0;
+  return true;
+}
+
+
+// PV of tile `pi` (held in stage `pst`): O^T[512 x NHC] (+)= V^T . P^T, then hand the stage
+// back and signal pv_done.  An all-padding tile (live == false) has P == 0 and skips the
+// MMAs.  o_init tracks whether O already holds this segment's sum.
+template <int NHC>
+__device__ __forceinline__ bool issue_pv(const Waiter& wait, uint32_t bar0, uint32_t sbase,
+                                         uint32_t tmem, int64_t pi, int pst, bool first,
+                                         bool live, bool& o_init) {
+  using C = Cfg<NHC>;
+  constexpr uint32_t kIdescPV = idesc_bf16(128, NHC, true);
+  if (!wait(bar0 + 8u * (uint32_t)(B_PF + (int)(pi & 1)), (uint32_t)((pi >> 1) & 1))) return false;
+  ptx::tc_fence_after();
+  if (first) o_init = false;
+  if (live) {
+    const uint32_t kv = sbase + (uint32_t)(C::OFF_KV + pst * kStageBytes);
+    const uint32_t pb = sbase + (uint32_t)(C::OFF_P + (int)(pi % C::PBUF) * C::P_BYTES);
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+      for (int ks = 0; ks < kPVSteps; ++ks)
+        ptx::umma_bf16(tmem + (uint32_t)(C::O_COL + mt * NHC),
+                       sdesc(kv + (uint32_t)(2 * mt * kRegion + ks * 2048), kRegion, 1024),
+                       sdesc(pb + (uint32_t)(ks * 32), 16, 1024), kIdescPV,
+                       (o_init || ks > 0) ? 1u : 0u);
+    o_init = true;
+  }
+  ptx::umma_commit(bar0 + 8u * (uint32_t)(B_KVE + pst));
+  ptx::umma_commit(bar0 + 8u * (uint32_t)(B_PD + (int)(pi & 1)));
   return true;
 }
 
@@ -220,7 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sgen + C::OFF_MISC);
   uint64_t* masks = reinterpret_cast<uint64_t*>(sgen + C::OFF_MASK);  // [STAGES][producer warp]
   float* red = reinterpret_cast<float*>(sgen + C::OFF_RED);
-  auto bar = [&](int k) -> uint32_t { return sbase + (uint32_t)C::OFF_BAR + 8u * (uint32_t)k; };
+  const uint32_t bar0 = sbase + (uint32_t)C::OFF_BAR;
+#define bar(k) (bar0 + 8u * (uint32_t)(k))
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -295,36 +349,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::regs_dec<kRegsLow>();
   } else if (warp < kSmWarp0 && warp != kMmaWarp) {
     // ------------------------------------------------------------------ gather producers
-    // Each tile is kUnits gather4 copies (16 groups of 4 slots x 9 d-blocks), ordered
+    // Each tile is kUnits gather4 copies (kGroups groups of 4 slots x 9 d-blocks), ordered
     // d-block first and dealt round-robin over the producer warps, so that all warps
     // issue in parallel and d-block 0 lands first.
     ptx::regs_dec<kRegsLow>();
     const int pw = warp - 1 - (warp >> 2);
     const int unit = lane * kProducerWarps + pw;
     const bool has_unit = unit < kUnits;
-    const int j = has_unit ? unit / 16 : 0;  // d-block
-    const int g = has_unit ? unit % 16 : 0;  // slots 4g .. 4g+3 of the tile
+    const int j = has_unit ? unit / kGroups : 0;  // d-block
+    const int g = has_unit ? unit % kGroups : 0;  // slots 4g .. 4g+3 of the tile
     const uint64_t policy = ptx::policy_evict_first();
-    // Slot ids of tile `uu` (unit index) for this lane's group; -1 past topk.
-    auto load_ids = [&](int64_t uu, int (&r)[4]) {
-      const int64_t rh = uu / p.tpr;
-      const int t = (int)(uu % p.tpr);
-      const int32_t* idx_row = p.idx + (rh / p.hg_count) * p.idx_sb;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int k = t * kBK + 4 * g + q;
-        r[q] = (has_unit && k < p.topk) ? __ldg(idx_row + k) : -1;
-      }
-    };
     bool ok = true;
-    int64_t last_issue[C::STAGES];
-    for (int k = 0; k < C::STAGES; ++k) last_issue[k] = -1;
+    int64_t n_issued = 0;  // tiles whose copies this warp has issued
     int cur[4], nxt[4];
-    if (u_lo < u_hi) load_ids(u_lo, cur);
+    if (u_lo < u_hi) load_slot_ids(p, u_lo, has_unit, g, cur);
     for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
       // The next tile's ids are requested before this tile waits for its stage, so
       // their load latency overlaps the wait instead of adding to it.
-      if (uu + 1 < u_hi) load_ids(uu + 1, nxt);
+      if (uu + 1 < u_hi) load_slot_ids(p, uu + 1, has_unit, g, nxt);
       const int stage = (int)(i % C::STAGES);
       uint64_t vbits = 0;
       bool bad = false;
@@ -347,12 +389,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mbar_arrive(bar(B_META + stage));
           if (pw == 0)
             for (int jj = 0; jj < kNDB; ++jj)
-              ptx::mbar_arrive_expect_tx(bar(kvf(stage, jj)), 16u * 512u);
+              ptx::mbar_arrive_expect_tx(bar(kvf(stage, jj)), (uint32_t)kGroups * 512u);
         }
       }
       ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
       if (!ok) break;
-      last_issue[stage] = i;
+      n_issued = i + 1;
       if (has_unit) {
         const uint32_t dst = sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes + j * kRegion + g * 512);
         const int4 rows = make_int4(cur[0], cur[1], cur[2], cur[3]);
@@ -367,10 +409,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0) {
       // Stop early: let every copy this warp issued land before the CTA exits.
       const Waiter drain{misc + 3, p.err};
-      for (int k = 0; k < C::STAGES; ++k)
-        if (last_issue[k] >= 0)
-          for (int jj = 0; jj < kNDB; ++jj)
-            drain(bar(kvf(k, jj)), (uint32_t)((last_issue[k] / C::STAGES) & 1));
+      for (int64_t li = n_issued - 1; li >= 0 && li >= n_issued - C::STAGES; --li)
+        for (int jj = 0; jj < kNDB; ++jj)
+          drain(bar(kvf((int)(li % C::STAGES), jj)), (uint32_t)((li / C::STAGES) & 1));
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -386,28 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t u = u_lo;
       Segment s;
       bool o_init = false;  // O holds this segment's sum (a live tile's PV was issued)
-      auto issue_pv = [&](int64_t pi, bool first, bool live) -> bool {
-        if (!wait(bar(B_PF + (int)(pi & 1)), (uint32_t)((pi >> 1) & 1))) return false;
-        ptx::tc_fence_after();
-        const int pst = (int)(pi % C::STAGES);
-        if (first) o_init = false;
-        if (live) {  // an all-padding tile has P == 0: its PV is skipped
-          const uint32_t kv = sbase + (uint32_t)(C::OFF_KV + pst * kStageBytes);
-          const uint32_t pb = sbase + (uint32_t)(C::OFF_P + (int)(pi % C::PBUF) * C::P_BYTES);
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-            for (int ks = 0; ks < kBK / 16; ++ks)
-              ptx::umma_bf16(tmem + (uint32_t)(C::O_COL + mt * NHC),
-                             sdesc(kv + (uint32_t)(2 * mt * kRegion + ks * 2048), kRegion, 1024),
-                             sdesc(pb + (uint32_t)(ks * 32), 16, 1024), kIdescPV,
-                             (o_init || ks > 0) ? 1u : 0u);
-          o_init = true;
-        }
-        ptx::umma_commit(bar(B_KVE + pst));
-        ptx::umma_commit(bar(B_PD + (int)(pi & 1)));
-        return true;
-      };
+      int64_t prev_i = -1;
+      int prev_stage = 0;
+      bool prev_first = false, prev_live = false;
       while (ok && next_segment(u, u_hi, p.tpr, s)) {
         const int qb = seg % C::QBUF;
         const uint32_t qbase = sbase + (uint32_t)(C::OFF_Q + qb * C::Q_BYTES);
@@ -423,16 +445,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int w = 0; w < kProducerWarps; ++w) m |= masks[stage * kProducerWarps + w];
           const bool live = m != 0ull;
-          // S^T[64 x NHC] = K[64 x 576] . Q[NHC x 576]^T, d-block by d-block as they land.
+          ptx::tc_fence_after();  // S(i & 1) was read by softmax(i - 2) before s_empty
+          // S^T[64 x NHC] = K[64 x 576] . Q[NHC x 576]^T, d-block by d-block as they land
+          // (a TMA full barrier orders the copy before the MMA; no tcgen05 fence needed).
           // An all-padding tile's scores are all masked: its MMAs are skipped, but its
-          // copies are still waited for before the stage is handed back.
+          // copies are still waited for before the stage is handed back.  With OVERLAP,
+          // the previous tile's PV is issued half-way through this score, so that the
+          // tensor core works on this tile while softmax(i-1) runs, without holding the
+          // previous stage for a whole extra score.
           const uint32_t kv = sbase + (uint32_t)(C::OFF_KV + stage * kStageBytes);
           const uint32_t d_s = tmem + (uint32_t)(C::S_COL + sb * NHC);
 #pragma unroll 1
-          for (int jj = 0; jj < kNDB && ok; ++jj) {
+          for (int jj = 0; jj < kNDB; ++jj) {
+            if (C::OVERLAP && jj == kPVSplit && prev_i >= 0) {
+              ok = issue_pv<NHC>(wait, bar0, sbase, tmem, prev_i, prev_stage, prev_first,
+                                 prev_live, o_init);
+              prev_i = -1;
+              if (!ok) break;
+            }
             ok = wait(bar(kvf(stage, jj)), kpar);
             if (!ok) break;
-            ptx::tc_fence_after();
             if (live) {
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
@@ -444,13 +476,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           ptx::umma_commit(bar(B_SF + sb));
           if (t == s.t1 - 1) ptx::umma_commit(bar(B_QE + qb));
-          // PV(i) right behind score(i): with two stages, releasing a stage early
-          // keeps more gathers in flight than overlapping score(i+1) with softmax(i).
-          ok = issue_pv(i, t == s.t0, live);
-          if (!ok) break;
+          if (C::OVERLAP) {
+            prev_i = i;
+            prev_stage = stage;
+            prev_first = (t == s.t0);
+            prev_live = live;
+            if (t == s.t1 - 1) {
+              // The segment's last PV is not deferred behind the next segment's first
+              // score (which waits for the next Q): the epilogue needs it now.
+              ok = issue_pv<NHC>(wait, bar0, sbase, tmem, prev_i, prev_stage, prev_first,
+                                 prev_live, o_init);
+              prev_i = -1;
+              if (!ok) break;
+            }
+          } else {
+            // PV(i) right behind score(i), so that the stage is handed back early.
+            ok = issue_pv<NHC>(wait, bar0, sbase, tmem, i, stage, t == s.t0, live, o_init);
+            if (!ok) break;
+          }
         }
         ++seg;
       }
+      if (ok && C::OVERLAP && prev_i >= 0)
+        ok = issue_pv<NHC>(wait, bar0, sbase, tmem, prev_i, prev_stage, prev_first, prev_live,
+                           o_init);
       if (!ok) {
         // Stop early: wait (bounded) until every MMA issued so far has retired.
         const Waiter drain{misc + 3, p.err};
@@ -468,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Score row (slot within the tile) of this lane: the M=64 accumulator keeps
     // rows 16*sp .. 16*sp+15 in lanes 0-15 of sub-partition sp.
     const int kv_row = 16 * sp + lane;
-    const bool row_lane = (lane < 16) && (kv_row < kBK);
+    const bool row_lane = lane < 16;                  // holds a score row (0..63)
+    const bool slot_lane = row_lane && kv_row < kBK;  // ... that is a slot of the tile
     int64_t i = 0;
     bool aborted = false;
     int64_t u = u_lo;
@@ -502,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_before();
         if (ok) ptx::mbar_arrive(bar(B_SE + sb));
-        const bool rv = row_lane && ((vmask >> kv_row) & 1ull);
+        const bool rv = slot_lane && ((vmask >> kv_row) & 1ull);
         float x[NHC];
         bool need = false;
 #pragma unroll
@@ -576,12 +626,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row_lane)
             *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(h, kv_row)) = __float2bfloat16_rn(pv);
         }
-        if (vmask != 0ull && row_lane && !rv) {
+        if (vmask != 0ull && slot_lane && !rv) {
           // A padded slot of a live tile: its P is 0, but 0 * (non-finite stale bytes)
-          // would poison the PV sum, so clear its value row (the 8 ckv d-blocks).
+          // would poison the PV sum, so clear its row in every d-block (the PV's last K
+          // step also reads rows kBK..63 of a d-block, i.e. rows 0..7 of the next one).
           uint8_t* row = sgen + C::OFF_KV + stage * kStageBytes + kv_row * 128;
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj)
+          for (int jj = 0; jj < kNDB; ++jj)
 #pragma unroll
             for (int q = 0; q < 8; ++q)
               *reinterpret_cast<uint4*>(row + jj * kRegion + q * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -637,13 +688,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (tid < NHC) {
-        const int h = tid;
+        // Thread tid writes head tid's scalars.  The element is picked with an unrolled
+        // select: indexing the register arrays by a run-time value would move them (and
+        // every access to them in the softmax loop) to local memory.
+        float mh = 0.f, lh = 0.f;
+#pragma unroll
+        for (int h = 0; h < NHC; ++h)
+          if (h == tid) {
+            mh = m_run[h];
+            lh = L[h];
+          }
         if (full) {
-          p.lse[b * p.lse_sb + (int64_t)(head0 + h) * p.lse_sh] =
-              L[h] > 0.f ? m_run[h] + ptx::lg2(L[h]) : -INFINITY;
+          p.lse[b * p.lse_sb + (int64_t)(head0 + tid) * p.lse_sh] =
+              lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         } else {
-          part[NHC * kDCkv + h] = m_run[h];
-          part[NHC * kDCkv + NHC + h] = L[h];
+          part[NHC * kDCkv + tid] = mh;
+          part[NHC * kDCkv + NHC + tid] = lh;
         }
       }
       ptx::tc_fence_before();
@@ -656,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, (uint32_t)C::TMEM_COLS);
   }
+#undef bar
 }
 
 
@@ -714,9 +775,16 @@ __global__ void __launch_bounds__(kDCkv) dsa_merge_kernel(const __grid_constant_
     const float y = Lt[h] > 0.f ? acc[h] / Lt[h] : 0.f;
     p.out[b * p.out_sb + (int64_t)(head0 + h) * p.out_sh + d] = __float2bfloat16_rn(y);
   }
-  if (d < 16)
-    p.lse[b * p.lse_sb + (int64_t)(head0 + d) * p.lse_sh] =
-        Lt[d] > 0.f ? M[d] + ptx::lg2(Lt[d]) : -INFINITY;
+  if (d < 16) {
+    float mh = 0.f, lh = 0.f;  // unrolled select keeps M / Lt in registers
+#pragma unroll
+    for (int h = 0; h < 16; ++h)
+      if (h == d) {
+        mh = M[h];
+        lh = Lt[h];
+      }
+    p.lse[b * p.lse_sb + (int64_t)(head0 + d) * p.lse_sh] = lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+  }
 }
 
 __global__ void selftest_wait_kernel(uint32_t* err, int64_t timeout_ns) {
