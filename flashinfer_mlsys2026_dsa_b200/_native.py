@@ -16,6 +16,7 @@ _lib = None
 DSA_OK = 0
 DEVERR_BAD_INDEX = 1
 DEVERR_TIMEOUT = 2
+ERR_SCRATCH_LIMIT = 7
 
 _c = ctypes
 _DECODE_ARGTYPES = [
@@ -35,6 +36,7 @@ _DECODE_ARGTYPES = [
 
 EXPORTED_SYMBOLS = (
     "dsa_sparse_mla_decode",
+    "dsa_sparse_mla_decode_noalloc",
     "dsa_sparse_mla_decode_workspace_size",
     "dsa_read_error_word",
     "dsa_selftest_bounded_wait",
@@ -68,6 +70,8 @@ def load(build_if_missing: bool = True):
             raise NativeLibraryError(f"cannot load {path}: {e}") from e
         lib.dsa_sparse_mla_decode.restype = _c.c_int
         lib.dsa_sparse_mla_decode.argtypes = _DECODE_ARGTYPES
+        lib.dsa_sparse_mla_decode_noalloc.restype = _c.c_int
+        lib.dsa_sparse_mla_decode_noalloc.argtypes = _DECODE_ARGTYPES[:-3] + [_c.c_void_p]
         lib.dsa_sparse_mla_decode_workspace_size.restype = _c.c_size_t
         lib.dsa_sparse_mla_decode_workspace_size.argtypes = [_c.c_int64, _c.c_int32, _c.c_int32,
                                                              _c.c_int32]

@@ -934,6 +934,9 @@ const char* dsa_status_string(int status) {
     case DSA_ERR_WORKSPACE: return "workspace missing or too small";
     case DSA_ERR_CUDA: return "CUDA runtime error";
     case DSA_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected the tensor";
+    case DSA_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the built-in no-allocation array holds "
+             "(use dsa_sparse_mla_decode with a caller workspace)";
     default: return "unknown status";
   }
 }
@@ -1062,3 +1065,125 @@ int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream)
 }
 
 }  // extern "C"
+
+// ============================================================ no-allocation entry point
+// Some callers cannot allocate device memory at the point where they decode: code that
+// runs inside another framework's allocator-controlled region, a plugin whose host
+// application forbids cudaMalloc on its hot path, or a process that must not grow its
+// device footprint after start-up.  dsa_sparse_mla_decode_noalloc() serves them: instead of
+// a caller-provided workspace it uses the fixed array below, which the CUDA module holds on
+// every device that loads this library until the process exits.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // error word + split-K partials
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int dsa_sparse_mla_decode_noalloc(
+    const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h, const void* q_pe,
+    int64_t q_pe_stride_b, int64_t q_pe_stride_h, const void* ckv_cache, int64_t ckv_slot_stride,
+    const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots,
+    const int32_t* sparse_indices, int64_t indices_stride_b, float sm_scale, void* output,
+    int64_t output_stride_b, int64_t output_stride_h, float* lse, int64_t lse_stride_b,
+    int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads, int32_t topk, void* stream) {
+  if (num_tokens < 0 || topk < 1 || num_slots < 1 || num_slots > INT32_MAX ||
+      num_tokens > INT32_MAX)
+    return DSA_ERR_INVALID_ARGUMENT;
+  const int nhc = nhc_for(num_heads);
+  if (nhc == 0) return DSA_ERR_UNSUPPORTED;
+  if (num_tokens == 0) return DSA_OK;
+  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (ckv_slot_stride < kDCkv || kpe_slot_stride < kDKpe || q_nope_stride_h < kDCkv ||
+      q_pe_stride_h < kDKpe || q_nope_stride_b < 1 || q_pe_stride_b < 1 || indices_stride_b < topk)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(q_nope) || !aligned16(q_pe) || !aligned16(ckv_cache) || !aligned16(kpe_cache) ||
+      (q_nope_stride_b * 2) % 16 || (q_nope_stride_h * 2) % 16 || (q_pe_stride_b * 2) % 16 ||
+      (q_pe_stride_h * 2) % 16 || (ckv_slot_stride * 2) % 16 || (kpe_slot_stride * 2) % 16)
+    return DSA_ERR_MISALIGNED;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return DSA_ERR_CUDA;
+
+  // The host cannot use g_noalloc_scratch as a device address: resolve the array's address
+  // on this device once (with this device current) and reuse it.
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* a = nullptr;
+      if (cudaGetSymbolAddress(&a, g_noalloc_scratch) != cudaSuccess || !a) return DSA_ERR_CUDA;
+      g_noalloc_addr[dev] = a;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+
+  const int hg = num_heads / nhc;
+  const int64_t num_rh = num_tokens * hg;
+  const int tpr = (topk + kBK - 1) / kBK;
+  const int64_t units = num_rh * tpr;
+  const int64_t grid = units < sms ? units : sms;
+  // Partials are laid out with this head group's own slot size (the kernel's stride).
+  const size_t slot_bytes = (size_t)(nhc * kDCkv + 2 * nhc) * 4;
+  const size_t need = 256 + (size_t)(2 * grid) * slot_bytes;
+  if (need > kNoAllocScratchBytes) return DSA_ERR_SCRATCH_LIMIT;
+
+  CUtensorMap m_ckv, m_kpe, m_qn, m_qp;
+  int rc;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)kDCkv, (cuuint64_t)num_slots};
+    cuuint64_t str[1] = {(cuuint64_t)ckv_slot_stride * 2};
+    cuuint32_t box[2] = {64, 1};
+    if ((rc = encode(&m_ckv, ckv_cache, 2, dims, str, box)) != DSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)kDKpe, (cuuint64_t)num_slots};
+    cuuint64_t str[1] = {(cuuint64_t)kpe_slot_stride * 2};
+    cuuint32_t box[2] = {64, 1};
+    if ((rc = encode(&m_kpe, kpe_cache, 2, dims, str, box)) != DSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kDCkv, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
+    cuuint64_t str[2] = {(cuuint64_t)q_nope_stride_h * 2, (cuuint64_t)q_nope_stride_b * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
+    if ((rc = encode(&m_qn, q_nope, 3, dims, str, box)) != DSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kDKpe, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
+    cuuint64_t str[2] = {(cuuint64_t)q_pe_stride_h * 2, (cuuint64_t)q_pe_stride_b * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
+    if ((rc = encode(&m_qp, q_pe, 3, dims, str, box)) != DSA_OK) return rc;
+  }
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  // The array keeps the previous call's bytes: the error word must start at zero; the
+  // partials are always written before they are read.
+  if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess) return DSA_ERR_CUDA;
+
+  Params prm;
+  prm.idx = sparse_indices;
+  prm.idx_sb = indices_stride_b;
+  prm.out = static_cast<__nv_bfloat16*>(output);
+  prm.out_sb = output_stride_b;
+  prm.out_sh = output_stride_h;
+  prm.lse = lse;
+  prm.lse_sb = lse_stride_b;
+  prm.lse_sh = lse_stride_h;
+  prm.num_slots = num_slots;
+  prm.units = units;
+  prm.hg_count = hg;
+  prm.topk = topk;
+  prm.tpr = tpr;
+  prm.scale_log2 = sm_scale * kLog2e;
+  prm.err = reinterpret_cast<uint32_t*>(ws);
+  prm.parts = reinterpret_cast<float*>(ws + 256);
+  switch (nhc) {
+    case 16: return launch<16>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
+    case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
+    default: return launch<64>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
+  }
+}

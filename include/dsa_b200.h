@@ -39,7 +39,8 @@ enum {
   DSA_ERR_MISALIGNED = 3,       /* pointer or stride violates the 16-byte TMA rule */
   DSA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
   DSA_ERR_CUDA = 5,             /* a CUDA runtime call or the launch failed */
-  DSA_ERR_DRIVER = 6            /* cuTensorMapEncodeTiled unavailable / rejected */
+  DSA_ERR_DRIVER = 6,           /* cuTensorMapEncodeTiled unavailable / rejected */
+  DSA_ERR_SCRATCH_LIMIT = 7     /* dsa_sparse_mla_decode_noalloc: over its fixed scratch */
 };
 
 /* Bits of the sticky device error word kept in the workspace. */
@@ -108,6 +109,40 @@ int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word
  * path without faulting or hanging the GPU.  No counterpart in the reference.
  */
 int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream);
+
+/*
+ * The same decode for callers that cannot allocate device memory (code running under
+ * another framework's allocator, a host application that forbids cudaMalloc on its
+ * decode path, a process whose device footprint must not grow after start-up).  No
+ * counterpart in the reference: its entry point (fused.py:150) is called with outputs
+ * preallocated and needs no scratch; this library's split-K partials normally live in
+ * the caller's workspace.
+ *
+ * Arguments are those of dsa_sparse_mla_decode() without the workspace.  Instead of a
+ * workspace the call uses a fixed 16 MiB array that the library's CUDA module holds on
+ * every device that loads it, until the process exits; the call itself allocates
+ * nothing (no cudaMalloc, cudaFree or allocating library routine).
+ *   - The first call on a device resolves the array's device address (once per device,
+ *     with that device current) and keeps it for later calls.
+ *   - Limit: the split-K partials must fit in the array: 256 B + 2 x (SMs) x 32,896 B
+ *     for num_heads 16 (9.7 MB on a 148-SM B200).  Larger head groups (num_heads 32, 64,
+ *     128) exceed it and return DSA_ERR_SCRATCH_LIMIT; use dsa_sparse_mla_decode.
+ *   - Every call on a device shares the array and finds the previous call's bytes there:
+ *     the call clears the error word it uses (device error bits are not reported by this
+ *     entry point) and always writes the partials before reading them.  Calls that
+ *     overlap on the GPU (different streams, or concurrent host threads) race on the
+ *     array; order them on one stream.
+ */
+int dsa_sparse_mla_decode_noalloc(const void* q_nope, int64_t q_nope_stride_b,
+                                  int64_t q_nope_stride_h, const void* q_pe,
+                                  int64_t q_pe_stride_b, int64_t q_pe_stride_h,
+                                  const void* ckv_cache, int64_t ckv_slot_stride,
+                                  const void* kpe_cache, int64_t kpe_slot_stride,
+                                  int64_t num_slots, const int32_t* sparse_indices,
+                                  int64_t indices_stride_b, float sm_scale, void* output,
+                                  int64_t output_stride_b, int64_t output_stride_h, float* lse,
+                                  int64_t lse_stride_b, int64_t lse_stride_h, int64_t num_tokens,
+                                  int32_t num_heads, int32_t topk, void* stream);
 
 /* Human-readable text of a status code (static storage). */
 const char* dsa_status_string(int status);
