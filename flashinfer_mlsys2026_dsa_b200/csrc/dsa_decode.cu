@@ -808,6 +808,11 @@ __global__ void selftest_wait_kernel(uint32_t* err, int64_t timeout_ns) {
   __syncthreads();
 }
 
+}  // namespace dsa
+
+#include "dsa_decode_h16.cuh"
+
+namespace dsa {
 // ====================================================================== host side
 namespace {
 
@@ -834,6 +839,7 @@ constexpr int kMaxDevices = 64;
 
 struct DeviceState {
   int sms = 0;
+  int pairs = 0;  // co-resident two-CTA clusters of the 16-head kernel
   bool attr_done[4] = {false, false, false, false};
 };
 std::mutex g_mu;
@@ -850,6 +856,36 @@ int device_sms(int dev) {
   return g_dev[dev].sms;
 }
 
+// Sets the 16-head kernel's shared-memory attribute and returns how many of its
+// clusters fit on the device at once (the persistent grid's size), 0 on error.
+int device_pairs(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  DeviceState& d = g_dev[dev];
+  if (d.pairs == 0) {
+    // The kernel re-splits its register pool per warpgroup (setmaxnreg); refuse a build
+    // whose pool is too small for that split, which would stall.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, h16::dsa_decode_h16_kernel) != cudaSuccess) return 0;
+    if ((int64_t)fa.numRegs * h16::kThreads < 256 * (int64_t)(h16::kRegsLow + h16::kRegsHigh))
+      return 0;
+    if (cudaFuncSetAttribute(h16::dsa_decode_h16_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             h16::SMEM_BYTES) != cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)(d.sms > 0 ? d.sms : 148), 1, 1);
+    cfg.blockDim = dim3(h16::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = h16::SMEM_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, h16::dsa_decode_h16_kernel, &cfg) != cudaSuccess ||
+        n <= 0)
+      return 0;
+    d.pairs = n;
+  }
+  return d.pairs;
+}
+
 int nhc_for(int heads) {
   switch (heads) {
     case 16: return 16;
@@ -864,8 +900,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Workspace layout, fixed for a device so that calls of any shape can share it:
 //   [0, 256)            header (word 0: sticky device error bits)
-//   [256, 256 + parts)  split-K partials: 2 slots per decode CTA, each sized for the
-//                       widest head group (64 heads) whatever this call's group width
+//   [256, 256 + parts)  split-K partials: 2 slots per decode CTA (or CTA pair), each
+//                       sized for the widest head group (64 heads)
 struct WsLayout {
   size_t parts_off, total;
 };
@@ -880,14 +916,13 @@ WsLayout ws_layout(int sms) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-           const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+           const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return DSA_ERR_DRIVER;
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
-                  dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? DSA_OK : DSA_ERR_DRIVER;
 }
 
@@ -914,6 +949,143 @@ int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn
   dsa_decode_kernel<NHC><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ckv, kpe, qn, qp, prm);
   if (grid > 1) dsa_merge_kernel<NHC><<<dim3(grid - 1, NHC / 16), kDCkv, 0, stream>>>(prm, grid);
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+// One decode call: the C-ABI arguments without the workspace.
+struct DecodeArgs {
+  const void* q_nope;
+  int64_t qn_sb, qn_sh;
+  const void* q_pe;
+  int64_t qp_sb, qp_sh;
+  const void* ckv;
+  int64_t ckv_ss;
+  const void* kpe;
+  int64_t kpe_ss;
+  int64_t num_slots;
+  const int32_t* idx;
+  int64_t idx_sb;
+  float sm_scale;
+  void* out;
+  int64_t out_sb, out_sh;
+  float* lse;
+  int64_t lse_sb, lse_sh;
+  int64_t num_tokens;
+  int32_t num_heads;
+  int32_t topk;
+};
+
+int check_args(const DecodeArgs& a) {
+  if (a.num_tokens < 0 || a.topk < 1 || a.num_slots < 1 || a.num_slots > INT32_MAX ||
+      a.num_tokens > INT32_MAX)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (nhc_for(a.num_heads) == 0) return DSA_ERR_UNSUPPORTED;
+  if (a.num_tokens == 0) return DSA_OK;
+  if (!a.q_nope || !a.q_pe || !a.ckv || !a.kpe || !a.idx || !a.out || !a.lse)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (a.ckv_ss < kDCkv || a.kpe_ss < kDKpe || a.qn_sh < kDCkv || a.qp_sh < kDKpe || a.qn_sb < 1 ||
+      a.qp_sb < 1 || a.idx_sb < a.topk)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a.q_nope) || !aligned16(a.q_pe) || !aligned16(a.ckv) || !aligned16(a.kpe) ||
+      (a.qn_sb * 2) % 16 || (a.qn_sh * 2) % 16 || (a.qp_sb * 2) % 16 || (a.qp_sh * 2) % 16 ||
+      (a.ckv_ss * 2) % 16 || (a.kpe_ss * 2) % 16)
+    return DSA_ERR_MISALIGNED;
+  return DSA_OK;
+}
+
+// Which kernel a call runs, its persistent grid and the scratch it needs.
+struct Plan {
+  bool pair = false;  // the 16-head two-CTA-cluster kernel
+  int nhc = 0;
+  int tpr = 0;
+  int64_t units = 0;
+  int grid = 0;       // CTAs (generic kernel) or clusters (pair kernel)
+  size_t need = 0;    // bytes of error header + partials
+};
+
+int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
+  const int sms = device_sms(dev);
+  if (sms <= 0) return DSA_ERR_CUDA;
+  pl.nhc = nhc_for(a.num_heads);
+  pl.pair = (pl.nhc == 16);
+  const int hg = a.num_heads / pl.nhc;
+  const int tile = pl.pair ? h16::kTS : kBK;
+  pl.tpr = (a.topk + tile - 1) / tile;
+  pl.units = a.num_tokens * hg * (int64_t)pl.tpr;
+  int cap = sms;
+  if (pl.pair) {
+    cap = device_pairs(dev);
+    if (cap <= 0) return DSA_ERR_CUDA;
+  }
+  pl.grid = (int)(pl.units < cap ? pl.units : cap);
+  const size_t slot_bytes = (size_t)(pl.nhc * kDCkv + 2 * pl.nhc) * 4;
+  pl.need = 256 + (size_t)(2 * pl.grid) * slot_bytes;
+  return DSA_OK;
+}
+
+int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, int dev, cudaStream_t st) {
+  const int nhc = pl.nhc;
+  CUtensorMap m_ckv, m_kpe, m_qn, m_qp;
+  const cuuint32_t kpe_w = pl.pair ? 32 : 64;  // the pair kernel loads 32-wide kpe halves
+  const CUtensorMapSwizzle kpe_swz = pl.pair ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)kDCkv, (cuuint64_t)a.num_slots};
+    cuuint64_t str[1] = {(cuuint64_t)a.ckv_ss * 2};
+    cuuint32_t box[2] = {64, 1};
+    if ((rc = encode(&m_ckv, a.ckv, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != DSA_OK)
+      return rc;
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)kDKpe, (cuuint64_t)a.num_slots};
+    cuuint64_t str[1] = {(cuuint64_t)a.kpe_ss * 2};
+    cuuint32_t box[2] = {kpe_w, 1};
+    if ((rc = encode(&m_kpe, a.kpe, 2, dims, str, box, kpe_swz)) != DSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kDCkv, (cuuint64_t)a.num_heads, (cuuint64_t)a.num_tokens};
+    cuuint64_t str[2] = {(cuuint64_t)a.qn_sh * 2, (cuuint64_t)a.qn_sb * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
+    if ((rc = encode(&m_qn, a.q_nope, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != DSA_OK)
+      return rc;
+  }
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)kDKpe, (cuuint64_t)a.num_heads, (cuuint64_t)a.num_tokens};
+    cuuint64_t str[2] = {(cuuint64_t)a.qp_sh * 2, (cuuint64_t)a.qp_sb * 2};
+    cuuint32_t box[3] = {kpe_w, (cuuint32_t)nhc, 1};
+    if ((rc = encode(&m_qp, a.q_pe, 3, dims, str, box, kpe_swz)) != DSA_OK) return rc;
+  }
+  Params prm;
+  prm.idx = a.idx;
+  prm.idx_sb = a.idx_sb;
+  prm.out = static_cast<__nv_bfloat16*>(a.out);
+  prm.out_sb = a.out_sb;
+  prm.out_sh = a.out_sh;
+  prm.lse = a.lse;
+  prm.lse_sb = a.lse_sb;
+  prm.lse_sh = a.lse_sh;
+  prm.num_slots = a.num_slots;
+  prm.units = pl.units;
+  prm.hg_count = a.num_heads / nhc;
+  prm.topk = a.topk;
+  prm.tpr = pl.tpr;
+  prm.scale_log2 = a.sm_scale * kLog2e;
+  prm.err = reinterpret_cast<uint32_t*>(ws);
+  prm.parts = reinterpret_cast<float*>(ws + 256);
+  if (pl.pair) {
+    h16::dsa_decode_h16_kernel<<<2 * pl.grid, h16::kThreads, h16::SMEM_BYTES, st>>>(
+        m_ckv, m_kpe, m_qn, m_qp, prm);
+    if (pl.grid > 1) dsa_merge_kernel<16><<<dim3(pl.grid - 1, 1), kDCkv, 0, st>>>(prm, pl.grid);
+    return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+  }
+  switch (nhc) {
+    case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, pl.grid, dev, st);
+    default: return launch<64>(m_ckv, m_kpe, m_qn, m_qp, prm, pl.grid, dev, st);
+  }
+}
+
+int current_device(int& dev) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
+  return DSA_OK;
 }
 
 }  // namespace
@@ -959,87 +1131,22 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
                           int64_t output_stride_h, float* lse, int64_t lse_stride_b,
                           int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads,
                           int32_t topk, void* workspace, size_t workspace_bytes, void* stream) {
-  if (num_tokens < 0 || topk < 1 || num_slots < 1 || num_slots > INT32_MAX ||
-      num_tokens > INT32_MAX)
-    return DSA_ERR_INVALID_ARGUMENT;
-  const int nhc = nhc_for(num_heads);
-  if (nhc == 0) return DSA_ERR_UNSUPPORTED;
-  if (num_tokens == 0) return DSA_OK;
-  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse)
-    return DSA_ERR_INVALID_ARGUMENT;
-  if (ckv_slot_stride < kDCkv || kpe_slot_stride < kDKpe || q_nope_stride_h < kDCkv ||
-      q_pe_stride_h < kDKpe || q_nope_stride_b < 1 || q_pe_stride_b < 1 || indices_stride_b < topk)
-    return DSA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(q_nope) || !aligned16(q_pe) || !aligned16(ckv_cache) || !aligned16(kpe_cache) ||
-      (q_nope_stride_b * 2) % 16 || (q_nope_stride_h * 2) % 16 || (q_pe_stride_b * 2) % 16 ||
-      (q_pe_stride_h * 2) % 16 || (ckv_slot_stride * 2) % 16 || (kpe_slot_stride * 2) % 16)
-    return DSA_ERR_MISALIGNED;
-
+  const DecodeArgs a{q_nope,          q_nope_stride_b, q_nope_stride_h, q_pe,
+                     q_pe_stride_b,   q_pe_stride_h,   ckv_cache,       ckv_slot_stride,
+                     kpe_cache,       kpe_slot_stride, num_slots,       sparse_indices,
+                     indices_stride_b, sm_scale,       output,          output_stride_b,
+                     output_stride_h, lse,             lse_stride_b,    lse_stride_h,
+                     num_tokens,      num_heads,       topk};
+  int rc = check_args(a);
+  if (rc != DSA_OK || num_tokens == 0) return rc;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
+  if ((rc = current_device(dev)) != DSA_OK) return rc;
   const int sms = device_sms(dev);
   if (sms <= 0) return DSA_ERR_CUDA;
-
-  const int hg = num_heads / nhc;
-  const int64_t num_rh = num_tokens * hg;
-  const int tpr = (topk + kBK - 1) / kBK;
-  const int64_t units = num_rh * tpr;
-  const int64_t grid = units < sms ? units : sms;
-  const WsLayout wl = ws_layout(sms);
-  if (!workspace || workspace_bytes < wl.total) return DSA_ERR_WORKSPACE;
-
-  CUtensorMap m_ckv, m_kpe, m_qn, m_qp;
-  int rc;
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)kDCkv, (cuuint64_t)num_slots};
-    cuuint64_t str[1] = {(cuuint64_t)ckv_slot_stride * 2};
-    cuuint32_t box[2] = {64, 1};
-    if ((rc = encode(&m_ckv, ckv_cache, 2, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)kDKpe, (cuuint64_t)num_slots};
-    cuuint64_t str[1] = {(cuuint64_t)kpe_slot_stride * 2};
-    cuuint32_t box[2] = {64, 1};
-    if ((rc = encode(&m_kpe, kpe_cache, 2, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)kDCkv, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
-    cuuint64_t str[2] = {(cuuint64_t)q_nope_stride_h * 2, (cuuint64_t)q_nope_stride_b * 2};
-    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
-    if ((rc = encode(&m_qn, q_nope, 3, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)kDKpe, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
-    cuuint64_t str[2] = {(cuuint64_t)q_pe_stride_h * 2, (cuuint64_t)q_pe_stride_b * 2};
-    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
-    if ((rc = encode(&m_qp, q_pe, 3, dims, str, box)) != DSA_OK) return rc;
-  }
-
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  Params prm;
-  prm.idx = sparse_indices;
-  prm.idx_sb = indices_stride_b;
-  prm.out = static_cast<__nv_bfloat16*>(output);
-  prm.out_sb = output_stride_b;
-  prm.out_sh = output_stride_h;
-  prm.lse = lse;
-  prm.lse_sb = lse_stride_b;
-  prm.lse_sh = lse_stride_h;
-  prm.num_slots = num_slots;
-  prm.units = units;
-  prm.hg_count = hg;
-  prm.topk = topk;
-  prm.tpr = tpr;
-  prm.scale_log2 = sm_scale * kLog2e;
-  prm.err = reinterpret_cast<uint32_t*>(ws);
-  prm.parts = reinterpret_cast<float*>(ws + wl.parts_off);
-
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (nhc) {
-    case 16: return launch<16>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-    case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-    default: return launch<64>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-  }
+  if (!workspace || workspace_bytes < ws_layout(sms).total) return DSA_ERR_WORKSPACE;
+  Plan pl;
+  if ((rc = make_plan(a, dev, pl)) != DSA_OK) return rc;
+  return run_plan(a, pl, static_cast<uint8_t*>(workspace), dev, static_cast<cudaStream_t>(stream));
 }
 
 int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word) {
@@ -1087,26 +1194,19 @@ extern "C" int dsa_sparse_mla_decode_noalloc(
     const int32_t* sparse_indices, int64_t indices_stride_b, float sm_scale, void* output,
     int64_t output_stride_b, int64_t output_stride_h, float* lse, int64_t lse_stride_b,
     int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads, int32_t topk, void* stream) {
-  if (num_tokens < 0 || topk < 1 || num_slots < 1 || num_slots > INT32_MAX ||
-      num_tokens > INT32_MAX)
-    return DSA_ERR_INVALID_ARGUMENT;
-  const int nhc = nhc_for(num_heads);
-  if (nhc == 0) return DSA_ERR_UNSUPPORTED;
-  if (num_tokens == 0) return DSA_OK;
-  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !sparse_indices || !output || !lse)
-    return DSA_ERR_INVALID_ARGUMENT;
-  if (ckv_slot_stride < kDCkv || kpe_slot_stride < kDKpe || q_nope_stride_h < kDCkv ||
-      q_pe_stride_h < kDKpe || q_nope_stride_b < 1 || q_pe_stride_b < 1 || indices_stride_b < topk)
-    return DSA_ERR_INVALID_ARGUMENT;
-  if (!aligned16(q_nope) || !aligned16(q_pe) || !aligned16(ckv_cache) || !aligned16(kpe_cache) ||
-      (q_nope_stride_b * 2) % 16 || (q_nope_stride_h * 2) % 16 || (q_pe_stride_b * 2) % 16 ||
-      (q_pe_stride_h * 2) % 16 || (ckv_slot_stride * 2) % 16 || (kpe_slot_stride * 2) % 16)
-    return DSA_ERR_MISALIGNED;
-
+  const DecodeArgs a{q_nope,          q_nope_stride_b, q_nope_stride_h, q_pe,
+                     q_pe_stride_b,   q_pe_stride_h,   ckv_cache,       ckv_slot_stride,
+                     kpe_cache,       kpe_slot_stride, num_slots,       sparse_indices,
+                     indices_stride_b, sm_scale,       output,          output_stride_b,
+                     output_stride_h, lse,             lse_stride_b,    lse_stride_h,
+                     num_tokens,      num_heads,       topk};
+  int rc = check_args(a);
+  if (rc != DSA_OK || num_tokens == 0) return rc;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
-  const int sms = device_sms(dev);
-  if (sms <= 0) return DSA_ERR_CUDA;
+  if ((rc = current_device(dev)) != DSA_OK) return rc;
+  Plan pl;
+  if ((rc = make_plan(a, dev, pl)) != DSA_OK) return rc;
+  if (pl.need > kNoAllocScratchBytes) return DSA_ERR_SCRATCH_LIMIT;
 
   // The host cannot use g_noalloc_scratch as a device address: resolve the array's address
   // on this device once (with this device current) and reuse it.
@@ -1114,76 +1214,15 @@ extern "C" int dsa_sparse_mla_decode_noalloc(
   {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     if (!g_noalloc_addr[dev]) {
-      void* a = nullptr;
-      if (cudaGetSymbolAddress(&a, g_noalloc_scratch) != cudaSuccess || !a) return DSA_ERR_CUDA;
-      g_noalloc_addr[dev] = a;
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DSA_ERR_CUDA;
+      g_noalloc_addr[dev] = p;
     }
     scratch = g_noalloc_addr[dev];
   }
-
-  const int hg = num_heads / nhc;
-  const int64_t num_rh = num_tokens * hg;
-  const int tpr = (topk + kBK - 1) / kBK;
-  const int64_t units = num_rh * tpr;
-  const int64_t grid = units < sms ? units : sms;
-  // Partials are laid out with this head group's own slot size (the kernel's stride).
-  const size_t slot_bytes = (size_t)(nhc * kDCkv + 2 * nhc) * 4;
-  const size_t need = 256 + (size_t)(2 * grid) * slot_bytes;
-  if (need > kNoAllocScratchBytes) return DSA_ERR_SCRATCH_LIMIT;
-
-  CUtensorMap m_ckv, m_kpe, m_qn, m_qp;
-  int rc;
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)kDCkv, (cuuint64_t)num_slots};
-    cuuint64_t str[1] = {(cuuint64_t)ckv_slot_stride * 2};
-    cuuint32_t box[2] = {64, 1};
-    if ((rc = encode(&m_ckv, ckv_cache, 2, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)kDKpe, (cuuint64_t)num_slots};
-    cuuint64_t str[1] = {(cuuint64_t)kpe_slot_stride * 2};
-    cuuint32_t box[2] = {64, 1};
-    if ((rc = encode(&m_kpe, kpe_cache, 2, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)kDCkv, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
-    cuuint64_t str[2] = {(cuuint64_t)q_nope_stride_h * 2, (cuuint64_t)q_nope_stride_b * 2};
-    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
-    if ((rc = encode(&m_qn, q_nope, 3, dims, str, box)) != DSA_OK) return rc;
-  }
-  {
-    cuuint64_t dims[3] = {(cuuint64_t)kDKpe, (cuuint64_t)num_heads, (cuuint64_t)num_tokens};
-    cuuint64_t str[2] = {(cuuint64_t)q_pe_stride_h * 2, (cuuint64_t)q_pe_stride_b * 2};
-    cuuint32_t box[3] = {64, (cuuint32_t)nhc, 1};
-    if ((rc = encode(&m_qp, q_pe, 3, dims, str, box)) != DSA_OK) return rc;
-  }
-
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(scratch);
   // The array keeps the previous call's bytes: the error word must start at zero; the
   // partials are always written before they are read.
-  if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess) return DSA_ERR_CUDA;
-
-  Params prm;
-  prm.idx = sparse_indices;
-  prm.idx_sb = indices_stride_b;
-  prm.out = static_cast<__nv_bfloat16*>(output);
-  prm.out_sb = output_stride_b;
-  prm.out_sh = output_stride_h;
-  prm.lse = lse;
-  prm.lse_sb = lse_stride_b;
-  prm.lse_sh = lse_stride_h;
-  prm.num_slots = num_slots;
-  prm.units = units;
-  prm.hg_count = hg;
-  prm.topk = topk;
-  prm.tpr = tpr;
-  prm.scale_log2 = sm_scale * kLog2e;
-  prm.err = reinterpret_cast<uint32_t*>(ws);
-  prm.parts = reinterpret_cast<float*>(ws + 256);
-  switch (nhc) {
-    case 16: return launch<16>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-    case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-    default: return launch<64>(m_ckv, m_kpe, m_qn, m_qp, prm, (int)grid, dev, st);
-  }
+  if (cudaMemsetAsync(scratch, 0, 4, st) != cudaSuccess) return DSA_ERR_CUDA;
+  return run_plan(a, pl, static_cast<uint8_t*>(scratch), dev, st);
 }

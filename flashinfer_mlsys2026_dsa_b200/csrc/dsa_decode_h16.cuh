@@ -1,0 +1,611 @@
+// DSA decode for 16 heads (one head group): a two-CTA cluster per pair of SMs.
+//
+// Why a pair: with 16 heads the score MMA is S^T[slots x 16] = K . Q^T, whose cost is
+// set by the number of MMA instructions (an M=128, N=16 MMA costs about as much as an
+// M=64 one), so a tile should be 128 rows of slots.  A whole 1152-byte slot per row,
+// three stages deep (enough to hide the ~2-3 us gather latency under load), does not
+// fit in one SM's shared memory.  So each CTA of the pair owns half of every slot:
+//   rank r: ckv columns [256r, 256r + 256) (four 64-wide d-blocks, 128-byte swizzle)
+//           and kpe columns [32r, 32r + 32) (one 32-wide block, 64-byte swizzle),
+// i.e. 576 bytes per slot, three 96-slot stages.  Each CTA computes a partial score
+// over its 288 columns; the two partials are swapped through distributed shared
+// memory and both CTAs add them (own + peer: IEEE addition commutes, so both hold
+// bit-identical scores and take identical softmax decisions).  Each CTA then runs
+// PV over its own 256 value columns: O^T[256 d x 16] += V^T . P^T.
+//
+// Per CTA (512 threads):
+//   warp 0        Q loader: the row's Q half (4 boxes of [16 x 64] + 1 of [16 x 32]).
+//   warps 1-5     gather producers, one per d-block (warp 5: the kpe half); lane g
+//                 issues one tile::gather4 (slots 4g..4g+3) per tile.
+//   warp 6        score MMA issuer: 18 MMAs (M=128, N=16) per tile.
+//   warp 7        PV MMA issuer: 12 MMAs (M=128, N=16) per tile.
+//                 Two issuers, because an issuer's own shared-memory accesses (its
+//                 barrier waits) queue behind the tensor core's operand reads; with one
+//                 issuer those stalls, not the tensor core, set the tile period.
+//   warps 8-15    softmax / epilogue: warp w reads TMEM lanes 32(w%4).. (slots) and
+//                 handles heads 8((w-8)/4) .. +7.
+// The work split (stream-K over (row, 96-slot tile) units per pair), the split-K
+// partial layout and the merge kernel are those of the generic kernel, with a pair in
+// place of a CTA.  Every wait is bounded.
+#pragma once
+
+namespace dsa {
+namespace h16 {
+
+constexpr int kTS = 96;                  // slots per tile; the score MMA is M=128 and its
+                                         // rows >= kTS read the next 4 KB (never used)
+constexpr int kNH = 16;
+constexpr int kBlk = 4;                  // 64-wide ckv d-blocks per CTA
+constexpr int kRB = kTS * 128;           // one ckv d-block region of a stage
+constexpr int kRK = kTS * 64;            // the 32-wide kpe region of a stage
+constexpr int kStageB = kBlk * kRB + kRK;
+constexpr int kStages = 3;
+constexpr int kGroups = kTS / 4;         // gather4 copies per d-block per tile
+constexpr int kPVKs = kTS / 16;          // K steps of one PV MMA chain
+constexpr int kQB = kBlk * 2048 + 1024;  // one Q buffer: 4 x [16 x 64] SW128 + [16 x 32] SW64
+constexpr int kPB = 4096;                // P^T [16 x 128 slots] bf16, SW128 K-major
+constexpr int kXB = kTS * kNH * 4;       // partial scores from the peer, fp32 [kTS][16]
+constexpr int OFF_KV = 0;
+constexpr int OFF_Q = kStages * kStageB;
+constexpr int OFF_P = OFF_Q + 2 * kQB;
+constexpr int OFF_X = OFF_P + 2 * kPB;
+constexpr int OFF_BAR = OFF_X + 2 * kXB;
+constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
+constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag
+constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][8 heads] floats
+constexpr int SMEM_USED = OFF_RED + 2 * 4 * 8 * 4;
+constexpr int SMEM_BYTES = SMEM_USED + 1024;
+constexpr int kThreads = 512;
+constexpr int kQWarp = 0;
+constexpr int kProd0 = 1;
+constexpr int kProdWarps = kBlk + 1;
+constexpr int kMmaWarp = 6;     // score issuer; also allocates TMEM
+constexpr int kPvWarp = 7;
+constexpr int kSm0 = 8;
+constexpr int kSmThreads = 256;
+constexpr uint32_t kNamedBar = 1;
+// Register split after launch (512 threads x 128 = 65536): warpgroups 0-1 (loader,
+// producers, MMA issuer) drop to kRegsLow, the two softmax warpgroups rise to kRegsHigh.
+constexpr uint32_t kRegsLow = 72;
+constexpr uint32_t kRegsHigh = 184;
+static_assert(256 * (kRegsLow + kRegsHigh) <= 65536, "register split exceeds the pool");
+constexpr int TMEM_COLS = 64;
+constexpr int S_COL = 0;   // two score buffers x 16 columns
+constexpr int O_COL = 32;  // two 128-d tiles x 16 columns
+constexpr uint32_t kSw128 = 2, kSw64 = 4;  // UMMA descriptor layout types
+constexpr int kSlotFloats = kNH * kDCkv + 2 * kNH;
+
+enum : int {
+  B_KVF = 0,    // [3] stage landed: one arrive (with its bytes) per producer warp; d-block
+                //     0's warp writes the tile's slot masks before it arrives
+  B_KVE = 3,    // [3] stage free (PV done)
+  B_QF = 6, B_QE = 8,
+  B_SF = 10, B_SE = 12,  // score buffer full / read
+  B_PF = 14, B_PD = 16,  // P written (+ O rescaled) / PV done
+  B_XF = 18,    // [2] the peer's partial scores are in X[b] (st.async complete_tx)
+  B_OF = 20,    // the epilogue has read O
+  B_DRAIN = 21, // [2] used only when an issuer stops early
+  B_COUNT = 23
+};
+// X[b] needs no "empty" barrier: the peer writes X[b] for tile i + 2 only after it has
+// received this CTA's partial of tile i + 1, which this CTA sends after it has read
+// X[b] for tile i (tiles are processed in order on both sides).
+
+static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && kStageB % 1024 == 0 && kQB % 1024 == 0,
+              "128-byte swizzle atoms need 1024-byte alignment");
+static_assert((kBlk * kRB) % 512 == 0 && (kBlk * 2048) % 512 == 0,
+              "64-byte swizzle atoms need 512-byte alignment");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(B_COUNT * 8 <= 512, "barrier block");
+static_assert(kTS % 16 == 0 && kTS <= 128 && kGroups <= 32, "tile shape");
+static_assert(kStages * 4 * 4 <= 64, "mask words");
+
+__device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                         uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)layout << 61);
+}
+
+__device__ __forceinline__ void slot_ids(const Params& p, int64_t uu, bool has, int g,
+                                         int (&r)[4]) {
+  const int64_t row = uu / p.tpr;
+  const int t = (int)(uu % p.tpr);
+  const int32_t* ir = p.idx + row * p.idx_sb;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int k = t * kTS + 4 * g + e;
+    r[e] = (has && k < p.topk) ? __ldg(ir + k) : -1;
+  }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    dsa_decode_h16_kernel(const __grid_constant__ CUtensorMap tm_ckv,
+                          const __grid_constant__ CUtensorMap tm_kpe,
+                          const __grid_constant__ CUtensorMap tm_qn,
+                          const __grid_constant__ CUtensorMap tm_qp,
+                          const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
+  volatile uint32_t* masks = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MASK);
+  float* red = reinterpret_cast<float*>(sgen + OFF_RED);
+  const uint32_t bar0 = sbase + (uint32_t)OFF_BAR;
+#define bar(k) (bar0 + 8u * (uint32_t)(k))
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(bar(B_KVF + s), kProdWarps);
+      ptx::mbar_init(bar(B_KVE + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar(B_QF + b), 1);
+      ptx::mbar_init(bar(B_QE + b), 1);
+      ptx::mbar_init(bar(B_SF + b), 1);
+      ptx::mbar_init(bar(B_SE + b), kSmThreads);
+      ptx::mbar_init(bar(B_PF + b), kSmThreads);
+      ptx::mbar_init(bar(B_PD + b), 1);
+      // X[b] is full once this CTA armed it (one arrive with the expected bytes) and the
+      // peer's st.async bytes landed; the peer's stores may come before the arming.
+      ptx::mbar_init(bar(B_XF + b), 1);
+    }
+    ptx::mbar_init(bar(B_OF), kSmThreads);
+    ptx::mbar_init(bar(B_DRAIN), 1);
+    ptx::mbar_init(bar(B_DRAIN + 1), 1);
+    misc[2] = 0;
+    misc[3] = 0;
+    ptx::fence_mbar_init();
+    ptx::mbar_arrive_expect_tx(bar(B_XF + 0), (uint32_t)kXB);
+    ptx::mbar_arrive_expect_tx(bar(B_XF + 1), (uint32_t)kXB);
+  }
+  if (warp == kQWarp && lane == 0) {
+    ptx::prefetch_tmap(&tm_ckv);
+    ptx::prefetch_tmap(&tm_kpe);
+    ptx::prefetch_tmap(&tm_qn);
+    ptx::prefetch_tmap(&tm_qp);
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(sbase + (uint32_t)OFF_MISC, (uint32_t)TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  // Both CTAs' barriers are initialised before either arrives on the other's.
+  ptx::tc_fence_before();
+  ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem = misc[0];
+
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t G = gridDim.x >> 1;
+  const int64_t u_lo = u_begin(pair, p.units, G);
+  const int64_t u_hi = u_begin(pair + 1, p.units, G);
+  const Waiter wait{misc + 2, p.err};
+
+  if (warp == kQWarp) {
+    // ------------------------------------------------------------------ Q loader
+    ptx::regs_dec<kRegsLow>();
+    if (lane == 0) {
+      int seg = 0;
+      int64_t u = u_lo;
+      Segment s;
+      while (next_segment(u, u_hi, p.tpr, s)) {
+        const int qb = seg & 1;
+        if (!wait(bar(B_QE + qb), (uint32_t)(((seg >> 1) & 1) ^ 1))) break;
+        ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)kQB);
+        const uint32_t qd = sbase + (uint32_t)(OFF_Q + qb * kQB);
+        const int b = (int)s.rh;
+        for (int j = 0; j < kBlk; ++j)
+          ptx::tma_load_3d(qd + (uint32_t)(j * 2048), &tm_qn, (int)(256 * rank) + 64 * j, 0, b,
+                           bar(B_QF + qb));
+        ptx::tma_load_3d(qd + (uint32_t)(kBlk * 2048), &tm_qp, (int)(32 * rank), 0, b,
+                         bar(B_QF + qb));
+        ++seg;
+      }
+      if (seg > 0) {
+        const Waiter drain{misc + 3, p.err};
+        drain(bar(B_QF + ((seg - 1) & 1)), (uint32_t)(((seg - 1) >> 1) & 1));
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kProd0 && warp < kProd0 + kProdWarps) {
+    // ------------------------------------------------------------------ gather producers
+    ptx::regs_dec<kRegsLow>();
+    const int blk = warp - kProd0;  // 0..3: ckv d-block of this CTA's half; 4: kpe half
+    const int g = lane;
+    const bool has = g < kGroups;
+    const bool is_kpe = blk == kBlk;
+    const uint32_t dst_off =
+        is_kpe ? (uint32_t)(kBlk * kRB + g * 256) : (uint32_t)(blk * kRB + g * 512);
+    const int col = is_kpe ? (int)(32 * rank) : (int)(256 * rank) + 64 * blk;
+    const uint32_t tile_bytes = (uint32_t)kGroups * (is_kpe ? 256u : 512u);
+    const CUtensorMap* map = is_kpe ? &tm_kpe : &tm_ckv;
+    const uint64_t policy = ptx::policy_evict_first();
+    bool ok = true;
+    int64_t n_issued = 0;
+    int cur[4], nxt[4];
+    if (u_lo < u_hi) slot_ids(p, u_lo, has, g, cur);
+    for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
+      if (uu + 1 < u_hi) slot_ids(p, uu + 1, has, g, nxt);
+      const int st = (int)(i % kStages);
+      uint32_t nib = 0;
+      bool bad = false;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (cur[e] < -1 || (int64_t)cur[e] >= p.num_slots) {
+          bad = true;
+          cur[e] = -1;
+        }
+        nib |= (cur[e] >= 0 ? 1u : 0u) << e;
+      }
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+      if (blk == 0) {
+        if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
+        const uint32_t sh = nib << (4 * (g & 7));
+        w0 = __reduce_or_sync(0xffffffffu, (g >> 3) == 0 ? sh : 0u);
+        w1 = __reduce_or_sync(0xffffffffu, (g >> 3) == 1 ? sh : 0u);
+        w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
+      }
+      if (lane == 0) {
+        ok = wait(bar(B_KVE + st), (uint32_t)(((i / kStages) & 1) ^ 1));
+        if (ok) {
+          if (blk == 0) {
+            masks[st * 4 + 0] = w0;
+            masks[st * 4 + 1] = w1;
+            masks[st * 4 + 2] = w2;
+            masks[st * 4 + 3] = w0 | w1 | w2;  // nonzero: the tile has a valid slot
+          }
+          ptx::mbar_arrive_expect_tx(bar(B_KVF + st), tile_bytes);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+      if (!ok) break;
+      n_issued = i + 1;
+      if (has)
+        ptx::tma_gather4(sbase + (uint32_t)(OFF_KV + st * kStageB) + dst_off, map, col,
+                         make_int4(cur[0], cur[1], cur[2], cur[3]), bar(B_KVF + st), policy);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) cur[e] = nxt[e];
+    }
+    if (!ok && lane == 0) {
+      const Waiter drain{misc + 3, p.err};
+      for (int64_t li = n_issued - 1; li >= 0 && li >= n_issued - kStages; --li)
+        drain(bar(B_KVF + (int)(li % kStages)), (uint32_t)((li / kStages) & 1));
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ score MMA issuer
+    ptx::regs_dec<kRegsLow>();
+    if (lane == 0) {
+      const Waiter wait{misc + 2, p.err, true};
+      constexpr uint32_t kIdS = idesc_bf16(128, kNH, false);
+      // Descriptors of offset 0; an operand at byte offset o adds o >> 4.
+      const uint64_t dk = desc(sbase + (uint32_t)OFF_KV, 16, 1024, kSw128);
+      const uint64_t dkp = desc(sbase + (uint32_t)(OFF_KV + kBlk * kRB), 16, 512, kSw64);
+      const uint64_t dq = desc(sbase + (uint32_t)OFF_Q, 16, 1024, kSw128);
+      const uint64_t dqp = desc(sbase + (uint32_t)(OFF_Q + kBlk * 2048), 16, 512, kSw64);
+      int64_t i = 0;
+      int seg = 0;
+      bool ok = true;
+      int64_t u = u_lo;
+      Segment s;
+      while (ok && next_segment(u, u_hi, p.tpr, s)) {
+        const int qb = seg & 1;
+        const uint64_t qo = (uint64_t)((qb * kQB) >> 4);
+        for (int t = s.t0; t < s.t1; ++t, ++i) {
+          const int st = (int)(i % kStages);
+          const int sb = (int)(i & 1);
+          if (t == s.t0) ok = wait(bar(B_QF + qb), (uint32_t)((seg >> 1) & 1));
+          ok = ok && wait(bar(B_SE + sb), (uint32_t)(((i >> 1) & 1) ^ 1));
+          ok = ok && wait(bar(B_KVF + st), (uint32_t)((i / kStages) & 1));
+          if (!ok) break;
+          // Partial S^T[128 x 16] over this CTA's 288 columns.  An all-padding tile
+          // skips its MMAs (its scores are all masked).
+          if (masks[st * 4 + 3] != 0u) {
+            ptx::tc_fence_after();
+            const uint32_t d_s = tmem + (uint32_t)(S_COL + 16 * sb);
+            const uint64_t ko = (uint64_t)((st * kStageB) >> 4);
+#pragma unroll
+            for (int j = 0; j < kBlk; ++j)
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                ptx::umma_bf16(d_s, dk + ko + (uint64_t)((j * kRB + ks * 32) >> 4),
+                               dq + qo + (uint64_t)((j * 2048 + ks * 32) >> 4), kIdS,
+                               (j | ks) ? 1u : 0u);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+              ptx::umma_bf16(d_s, dkp + ko + (uint64_t)((ks * 32) >> 4),
+                             dqp + qo + (uint64_t)((ks * 32) >> 4), kIdS, 1u);
+          }
+          ptx::umma_commit(bar(B_SF + sb));
+          if (t == s.t1 - 1) ptx::umma_commit(bar(B_QE + qb));
+        }
+        ++seg;
+      }
+      if (!ok) {
+        const Waiter drain{misc + 3, p.err};
+        ptx::umma_commit(bar(B_DRAIN));
+        drain(bar(B_DRAIN), 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPvWarp) {
+    // ------------------------------------------------------------------ PV MMA issuer
+    // O^T[256 x 16] (+)= V^T . P^T over this CTA's value half, once softmax has written
+    // P (and rescaled O); then the stage goes back to the producers.  The first PV of a
+    // segment waits until the previous segment's epilogue has read O.
+    ptx::regs_dec<kRegsLow>();
+    if (lane == 0) {
+      const Waiter wait{misc + 2, p.err, true};
+      constexpr uint32_t kIdPV = idesc_bf16(128, kNH, true);
+      const uint64_t dv = desc(sbase + (uint32_t)OFF_KV, kRB, 1024, kSw128);
+      const uint64_t dp = desc(sbase + (uint32_t)OFF_P, 16, 1024, kSw128);
+      int64_t j = 0;
+      int seg = 0;
+      bool ok = true;
+      bool o_init = false;
+      int64_t u = u_lo;
+      Segment s;
+      while (ok && next_segment(u, u_hi, p.tpr, s)) {
+        for (int t = s.t0; t < s.t1; ++t, ++j) {
+          const int st = (int)(j % kStages);
+          ok = wait(bar(B_PF + (int)(j & 1)), (uint32_t)((j >> 1) & 1));
+          if (ok && t == s.t0) {
+            if (seg > 0) ok = wait(bar(B_OF), (uint32_t)((seg - 1) & 1));
+            o_init = false;
+          }
+          if (!ok) break;
+          if (masks[st * 4 + 3] != 0u) {
+            ptx::tc_fence_after();
+            const uint64_t vo = (uint64_t)((st * kStageB) >> 4);
+            const uint64_t po = (uint64_t)(((int)(j & 1) * kPB) >> 4);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+              for (int ks = 0; ks < kPVKs; ++ks)
+                ptx::umma_bf16(tmem + (uint32_t)(O_COL + 16 * mt),
+                               dv + vo + (uint64_t)((2 * mt * kRB + ks * 2048) >> 4),
+                               dp + po + (uint64_t)(((ks >> 2) * 2048 + (ks & 3) * 32) >> 4),
+                               kIdPV, (o_init || ks > 0) ? 1u : 0u);
+            o_init = true;
+          }
+          ptx::umma_commit(bar(B_KVE + st));
+          ptx::umma_commit(bar(B_PD + (int)(j & 1)));
+        }
+        ++seg;
+      }
+      if (!ok) {
+        const Waiter drain{misc + 3, p.err};
+        ptx::umma_commit(bar(B_DRAIN + 1));
+        drain(bar(B_DRAIN + 1), 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue
+    ptx::regs_inc<kRegsHigh>();
+    const int qd = warp & 3;               // TMEM lane quadrant = slots 32qd .. 32qd+31
+    const int hh = (warp - kSm0) >> 2;     // heads 8hh .. 8hh+7
+    const int slot = 32 * qd + lane;
+    const bool slot_ok = slot < kTS;
+    const uint32_t lane_base = (uint32_t)(32 * qd) << 16;
+    const uint32_t x_own = sbase + (uint32_t)OFF_X;
+    const uint32_t x_peer = ptx::mapa(x_own, peer);
+    const uint32_t xf_peer = ptx::mapa(bar(B_XF), peer);
+    float* red_max = red;
+    int64_t i = 0;
+    bool aborted = false;
+    int64_t u = u_lo;
+    Segment s;
+    const int64_t first_rh = u_lo / p.tpr;
+    float m_run[8], l_part[8];
+    while (!aborted && next_segment(u, u_hi, p.tpr, s)) {
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        m_run[h] = -INFINITY;
+        l_part[h] = 0.f;
+      }
+      bool o_valid = false;
+      for (int t = s.t0; t < s.t1; ++t, ++i) {
+        const int st = (int)(i % kStages);
+        const int sb = (int)(i & 1);
+        bool ok = !aborted && wait(bar(B_KVF + st), (uint32_t)((i / kStages) & 1)) &&
+                  wait(bar(B_SF + sb), (uint32_t)((i >> 1) & 1));
+        const uint32_t mw = qd < 3 ? masks[st * 4 + qd] : 0u;
+        const bool live = masks[st * 4 + 3] != 0u;
+        const bool valid = slot_ok && ((mw >> lane) & 1u);
+        ptx::tc_fence_after();
+        uint32_t own[8];
+        ptx::tmem_ld8(tmem + lane_base + (uint32_t)(S_COL + 16 * sb + 8 * hh), own);
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        if (ok) ptx::mbar_arrive(bar(B_SE + sb));
+        // Swap partial scores with the peer: st.async ours into its X[sb] (completing its
+        // B_XF[sb] by bytes), then wait for its bytes in ours.
+        if (ok && slot_ok) {
+          const uint32_t a = x_peer + (uint32_t)(sb * kXB + slot * 64 + hh * 32);
+          const uint32_t xb = xf_peer + 8u * (uint32_t)sb;
+          ptx::st_async_v4(a, own[0], own[1], own[2], own[3], xb);
+          ptx::st_async_v4(a + 16u, own[4], own[5], own[6], own[7], xb);
+        }
+        ok = ok && wait(bar(B_XF + sb), (uint32_t)((i >> 1) & 1));
+        float x[8];
+        bool need = false;
+        {
+          float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb4 = pa;
+          if (slot_ok) {
+            const float* xs = reinterpret_cast<const float*>(sgen + OFF_X + sb * kXB + slot * 64 + hh * 32);
+            pa = *reinterpret_cast<const float4*>(xs);
+            pb4 = *reinterpret_cast<const float4*>(xs + 4);
+          }
+          // X[sb] is read: re-arm it for tile i + 2.
+          if (warp == kSm0 && lane == 0) ptx::mbar_arrive_expect_tx(bar(B_XF + sb), (uint32_t)kXB);
+          const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb4.x, pb4.y, pb4.z, pb4.w};
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            x[h] = valid ? (__uint_as_float(own[h]) + pr[h]) * p.scale_log2 : -INFINITY;
+            need |= x[h] > m_run[h] + kTau;
+          }
+        }
+        bool rescale = false;
+        if (ptx::bar_red_or(kNamedBar, kSmThreads, need || aborted || !ok)) {
+          if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !ok)) {
+            aborted = true;
+            break;
+          }
+          rescale = true;
+        }
+        if (rescale) {
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            float v = x[h];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0) red_max[(hh * 4 + qd) * 8 + h] = v;
+          }
+          ptx::bar_sync(kNamedBar, kSmThreads);
+          float alpha[8];
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const float* r4 = red_max + hh * 32 + h;
+            const float mt = fmaxf(fmaxf(r4[0], r4[8]), fmaxf(r4[16], r4[24]));
+            const float mn = fmaxf(m_run[h], mt);
+            alpha[h] = (m_run[h] == -INFINITY) ? 0.f : ptx::ex2(m_run[h] - mn);
+            l_part[h] *= alpha[h];
+            m_run[h] = mn;
+          }
+          if (o_valid) {
+            if (!wait(bar(B_PD + (int)((i - 1) & 1)), (uint32_t)(((i - 1) >> 1) & 1))) {
+              aborted = true;
+            } else {
+              ptx::tc_fence_after();
+#pragma unroll
+              for (int mt = 0; mt < 2; ++mt) {
+                const uint32_t ta = tmem + lane_base + (uint32_t)(O_COL + 16 * mt + 8 * hh);
+                uint32_t rr[8];
+                ptx::tmem_ld8(ta, rr);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 8; ++h)
+                  rr[h] = __float_as_uint(__uint_as_float(rr[h]) * alpha[h]);
+                ptx::tmem_st8(ta, rr);
+              }
+              ptx::tmem_wait_st();
+            }
+          }
+        }
+        if (aborted) continue;  // the next vote ends the loop for every thread
+        if (i >= 2 && !wait(bar(B_PD + (int)(i & 1)), (uint32_t)(((i - 2) >> 1) & 1))) {
+          aborted = true;
+          continue;
+        }
+        uint8_t* pbuf = sgen + OFF_P + (int)(i & 1) * kPB + (slot >> 6) * 2048;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
+          const float pv = ptx::ex2(x[h] - me);
+          l_part[h] += pv;
+          if (live && slot_ok)
+            *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(8 * hh + h, slot & 63)) =
+                __float2bfloat16_rn(pv);
+        }
+        if (live && slot_ok && !valid) {
+          // A padded slot of a live tile: P is 0, but 0 * (stale non-finite bytes) would
+          // poison the PV sum, so clear this slot's value row (d-blocks 2hh, 2hh+1).
+          uint8_t* row = sgen + OFF_KV + st * kStageB + slot * 128;
+#pragma unroll
+          for (int jb = 0; jb < 2; ++jb)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(row + (2 * hh + jb) * kRB + c * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(B_PF + (int)(i & 1)));
+        o_valid = o_valid || live;
+      }
+      // ---------------------------------------------------------------- epilogue
+      // Every thread votes here, also one that gave up after the last tile's vote.
+      const int64_t il = i - 1;
+      const bool okw = !aborted && wait(bar(B_PD + (int)(il & 1)), (uint32_t)((il >> 1) & 1));
+      if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !okw)) {
+        aborted = true;
+        break;
+      }
+      ptx::tc_fence_after();
+      float* red_sum = red;  // the max slots are free again: every thread passed the vote
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        float v = l_part[h];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) red_sum[(hh * 4 + qd) * 8 + h] = v;
+      }
+      ptx::bar_sync(kNamedBar, kSmThreads);
+      float L[8];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        const float* r4 = red_sum + hh * 32 + h;
+        L[h] = (r4[0] + r4[8]) + (r4[16] + r4[24]);
+      }
+      const int64_t b = s.rh;
+      const bool full = (s.t0 == 0 && s.t1 == p.tpr);
+      const int64_t pslot = 2 * pair + (s.rh == first_rh ? 0 : 1);
+      float* part = p.parts + pslot * kSlotFloats;
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t rr[8];
+        ptx::tmem_ld8(tmem + lane_base + (uint32_t)(O_COL + 16 * mt + 8 * hh), rr);
+        ptx::tmem_wait_ld();
+        const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const float o = __uint_as_float(rr[h]);
+          const int head = 8 * hh + h;
+          if (full)
+            p.out[b * p.out_sb + (int64_t)head * p.out_sh + d] =
+                __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
+          else
+            part[head * kDCkv + d] = o;
+        }
+      }
+      if (rank == 0 && qd == 0 && lane < 8) {
+        float mh = 0.f, lh = 0.f;  // unrolled select keeps m_run / L in registers
+#pragma unroll
+        for (int h = 0; h < 8; ++h)
+          if (h == lane) {
+            mh = m_run[h];
+            lh = L[h];
+          }
+        const int head = 8 * hh + lane;
+        if (full)
+          p.lse[b * p.lse_sb + (int64_t)head * p.lse_sh] = lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+        else {
+          part[kNH * kDCkv + head] = mh;
+          part[kNH * kDCkv + kNH + head] = lh;
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(B_OF));
+      // The sums are read; the next segment may reuse the slots after its first vote.
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  // Neither CTA leaves while the other may still write its exchange buffer.
+  ptx::cluster_sync();
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, (uint32_t)TMEM_COLS);
+  }
+#undef bar
+}
+
+}  // namespace h16
+}  // namespace dsa
