@@ -174,6 +174,22 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def max_over_ranks(values, world, device):
+    """Element-wise max of per-rank timings (ms) over all ranks of the default group."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def job_gbs(bytes_per_step, steps, world, max_ms):
+    """Whole-job throughput: the bytes of every rank's steps over the slowest rank's time."""
+    return bytes_per_step * steps * world / (max_ms * 1e-3) / 1e9
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -270,14 +286,10 @@ def run_ours(args):
         stream.synchronize()
     e2e_ms = f0.elapsed_time(f1)
 
-    times = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    dev_ms, e2e_ms = times.tolist()
+    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_ms], world, dev)
     ms_per_step = dev_ms / steps
-    total_bytes = bytes_per_step * steps * world
-    value = total_bytes / (dev_ms * 1e-3) / 1e9
-    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    value, e2e_value = job_gbs(bytes_per_step, steps, world, dev_ms), job_gbs(
+        bytes_per_step, steps, world, e2e_ms)
     peak, peak_kind = _peaks()
     per_call_gbs = bytes_per_step / (ms_per_step * 1e-3) / 1e9
 

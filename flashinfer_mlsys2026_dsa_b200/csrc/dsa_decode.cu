@@ -74,7 +74,7 @@ constexpr uint32_t kRegsLow = 80;     // producer / MMA warpgroups after the spl
 constexpr uint32_t kRegsHigh = 248;   // softmax warpgroup after the split
 constexpr float kTau = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+constexpr uint64_t kWaitCycles = 4000000000ull;  // ~2 s at the B200's ~2 GHz SM clock
 static_assert(kProducerWarps * 32 >= kUnits, "one gather per producer lane per tile");
 static_assert(kBK % 8 == 0 && kBK <= 64, "tile rows: whole 8-row swizzle atoms, 64-bit masks");
 
@@ -173,12 +173,12 @@ struct Waiter {
   }
   __device__ __forceinline__ bool operator()(uint32_t bar, uint32_t parity) const {
     if (poll(bar, parity)) return true;
-    const uint64_t t0 = ptx::globaltimer_ns();
+    const uint64_t t0 = ptx::cycles();
     for (uint32_t it = 1;; ++it) {
       if (poll(bar, parity)) return true;
       if ((it & 63u) == 0) {
         if (*abort_flag) return false;
-        if (ptx::globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        if (ptx::cycles() - t0 > kWaitCycles) {
           *abort_flag = 1;
           atomicOr(err, (uint32_t)DSA_DEVERR_TIMEOUT);
           return false;
@@ -310,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = misc[0];
+  ptx::launch_dependents();  // the merge grid may be scheduled; it waits for this grid
 
   const int64_t G = gridDim.x;
   const int64_t u_lo = u_begin(blockIdx.x, p.units, G);
@@ -728,6 +729,7 @@ template <int NHC>
 __global__ void __launch_bounds__(kDCkv) dsa_merge_kernel(const __grid_constant__ Params p,
                                                           int grid_main) {
   using C = Cfg<NHC>;
+  ptx::grid_dep_wait();  // launched early (programmatic serialization): wait for the decode
   const int64_t G = grid_main;
   const int64_t c = (int64_t)blockIdx.x + 1;
   if (c >= G) return;
@@ -797,9 +799,10 @@ __global__ void selftest_wait_kernel(uint32_t* err, int64_t timeout_ns) {
   __syncthreads();
   if (threadIdx.x == 0) {
     // Nothing ever arrives on this barrier: the wait must give up by itself.
-    const uint64_t t0 = ptx::globaltimer_ns();
+    // The bound counts SM cycles, two per requested nanosecond (~2 GHz clock).
+    const uint64_t t0 = ptx::cycles();
     while (!ptx::mbar_try_wait(b, 0)) {
-      if ((int64_t)(ptx::globaltimer_ns() - t0) > timeout_ns) {
+      if ((int64_t)(ptx::cycles() - t0) > 2 * timeout_ns) {
         atomicOr(err, (uint32_t)DSA_DEVERR_TIMEOUT);
         break;
       }
@@ -926,6 +929,25 @@ int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
   return r == CUDA_SUCCESS ? DSA_OK : DSA_ERR_DRIVER;
 }
 
+// The split-K merge for a decode grid of `grid` CTAs (or pairs), launched with
+// programmatic stream serialization so that its launch overlaps the decode's tail.
+template <int NHC>
+int launch_merge(const Params& prm, int grid, cudaStream_t stream) {
+  if (grid <= 1) return DSA_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(grid - 1), NHC / 16, 1);
+  cfg.blockDim = dim3(kDCkv, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, dsa_merge_kernel<NHC>, prm, grid) == cudaSuccess ? DSA_OK
+                                                                                   : DSA_ERR_CUDA;
+}
+
 template <int NHC>
 int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn,
            const CUtensorMap& qp, const Params& prm, int grid, int dev, cudaStream_t stream) {
@@ -947,8 +969,8 @@ int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn
     }
   }
   dsa_decode_kernel<NHC><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ckv, kpe, qn, qp, prm);
-  if (grid > 1) dsa_merge_kernel<NHC><<<dim3(grid - 1, NHC / 16), kDCkv, 0, stream>>>(prm, grid);
-  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  return launch_merge<NHC>(prm, grid, stream);
 }
 
 // One decode call: the C-ABI arguments without the workspace.
@@ -1074,8 +1096,8 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, int dev, cudaStre
   if (pl.pair) {
     h16::dsa_decode_h16_kernel<<<2 * pl.grid, h16::kThreads, h16::SMEM_BYTES, st>>>(
         m_ckv, m_kpe, m_qn, m_qp, prm);
-    if (pl.grid > 1) dsa_merge_kernel<16><<<dim3(pl.grid - 1, 1), kDCkv, 0, st>>>(prm, pl.grid);
-    return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+    return launch_merge<16>(prm, pl.grid, st);
   }
   switch (nhc) {
     case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, pl.grid, dev, st);

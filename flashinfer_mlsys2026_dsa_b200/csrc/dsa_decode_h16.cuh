@@ -78,15 +78,17 @@ constexpr int kSlotFloats = kNH * kDCkv + 2 * kNH;
 enum : int {
   B_KVF = 0,    // [3] stage landed: one arrive (with its bytes) per producer warp; d-block
                 //     0's warp writes the tile's slot masks before it arrives
-  B_KVE = 3,    // [3] stage free (PV done)
-  B_QF = 6, B_QE = 8,
-  B_SF = 10, B_SE = 12,  // score buffer full / read
-  B_PF = 14, B_PD = 16,  // P written (+ O rescaled) / PV done
-  B_XF = 18,    // [2] the peer's partial scores are in X[b] (st.async complete_tx)
-  B_OF = 20,    // the epilogue has read O
-  B_DRAIN = 21, // [2] used only when an issuer stops early
-  B_COUNT = 23
+  B_KVE = 3,    // [3][5] d-block region of a stage free again: the kpe region once the
+                //     score has read it, value d-blocks 0-1 / 2-3 once their PV half has
+  B_QF = 18, B_QE = 20,
+  B_SF = 22, B_SE = 24,  // score buffer full / read
+  B_PF = 26, B_PD = 28,  // P written (+ O rescaled) / PV done
+  B_XF = 30,    // [2] the peer's partial scores are in X[b] (st.async complete_tx)
+  B_OF = 32,    // the epilogue has read O
+  B_DRAIN = 33, // [2] used only when an issuer stops early
+  B_COUNT = 35
 };
+__host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * 5 + blk; }
 // X[b] needs no "empty" barrier: the peer writes X[b] for tile i + 2 only after it has
 // received this CTA's partial of tile i + 1, which this CTA sends after it has read
 // X[b] for tile i (tiles are processed in order on both sides).
@@ -142,7 +144,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(bar(B_KVF + s), kProdWarps);
-      ptx::mbar_init(bar(B_KVE + s), 1);
+      for (int j = 0; j < kProdWarps; ++j) ptx::mbar_init(bar(kve(s, j)), 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(bar(B_QF + b), 1);
@@ -179,6 +181,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem = misc[0];
+  ptx::launch_dependents();  // the merge grid may be scheduled; it waits for this grid
 
   const int64_t pair = blockIdx.x >> 1;
   const int64_t G = gridDim.x >> 1;
@@ -251,7 +254,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
       }
       if (lane == 0) {
-        ok = wait(bar(B_KVE + st), (uint32_t)(((i / kStages) & 1) ^ 1));
+        ok = wait(bar(kve(st, blk)), (uint32_t)(((i / kStages) & 1) ^ 1));
         if (ok) {
           if (blk == 0) {
             masks[st * 4 + 0] = w0;
@@ -322,6 +325,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                              dqp + qo + (uint64_t)((ks * 32) >> 4), kIdS, 1u);
           }
           ptx::umma_commit(bar(B_SF + sb));
+          ptx::umma_commit(bar(kve(st, kBlk)));  // the kpe region is read only by the score
           if (t == s.t1 - 1) ptx::umma_commit(bar(B_QE + qb));
         }
         ++seg;
@@ -364,16 +368,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t vo = (uint64_t)((st * kStageB) >> 4);
             const uint64_t po = (uint64_t)(((int)(j & 1) * kPB) >> 4);
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
               for (int ks = 0; ks < kPVKs; ++ks)
                 ptx::umma_bf16(tmem + (uint32_t)(O_COL + 16 * mt),
                                dv + vo + (uint64_t)((2 * mt * kRB + ks * 2048) >> 4),
                                dp + po + (uint64_t)(((ks >> 2) * 2048 + (ks & 3) * 32) >> 4),
                                kIdPV, (o_init || ks > 0) ? 1u : 0u);
+              // value d-blocks 2mt, 2mt+1 are free once this half's MMAs are done
+              ptx::umma_commit(bar(kve(st, 2 * mt)));
+              ptx::umma_commit(bar(kve(st, 2 * mt + 1)));
+            }
             o_init = true;
+          } else {
+            for (int jb = 0; jb < kBlk; ++jb) ptx::umma_commit(bar(kve(st, jb)));
           }
-          ptx::umma_commit(bar(B_KVE + st));
           ptx::umma_commit(bar(B_PD + (int)(j & 1)));
         }
         ++seg;

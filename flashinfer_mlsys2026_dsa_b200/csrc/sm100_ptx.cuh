@@ -51,9 +51,11 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ uint64_t globaltimer_ns() {
+// SM cycle counter.  Wait bounds count cycles: %globaltimer was seen to advance far
+// slower than real time on some B200 hosts, which would stretch a nanosecond bound.
+__device__ __forceinline__ uint64_t cycles() {
   uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
   return t;
 }
 
@@ -165,6 +167,18 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- programmatic launch
+// A dependent grid launched with programmatic stream serialization may start once every
+// CTA of this grid has executed launch_dependents; it must call grid_dep_wait before it
+// reads what this grid writes (the wait returns when this grid has completed and its
+// memory operations are visible).
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- clusters
