@@ -18,7 +18,11 @@ INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libdsa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = [os.path.join(CSRC, "dsa_decode.cu")]
-DEPS = SOURCES + [os.path.join(CSRC, "sm100_ptx.cuh"), os.path.join(INCLUDE, "dsa_b200.h")]
+# every source and header the library is built from (a change to any makes it stale)
+DEPS = sorted(
+    [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h"))]
+    + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h")]
+)
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -44,6 +44,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <utility>
 
 #include "dsa_b200.h"
 #include "sm100_ptx.cuh"
@@ -137,6 +138,7 @@ struct Params {
   float scale_log2;
   uint32_t* err;
   float* parts;
+  uint32_t* counters;  // split-K arrival counters (16-head kernel), zero between calls
 };
 
 // UMMA shared-memory descriptor, 128-byte swizzle, sm_100 (version 1).
@@ -310,7 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = misc[0];
-  ptx::launch_dependents();  // the merge grid may be scheduled; it waits for this grid
+  // Launched with programmatic stream serialization: the set-up above overlapped the
+  // previous grid's tail; nothing in global memory is touched before that grid is done.
+  ptx::grid_dep_wait();
+  ptx::launch_dependents();
 
   const int64_t G = gridDim.x;
   const int64_t u_lo = u_begin(blockIdx.x, p.units, G);
@@ -903,15 +908,21 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Workspace layout, fixed for a device so that calls of any shape can share it:
 //   [0, 256)            header (word 0: sticky device error bits)
-//   [256, 256 + parts)  split-K partials: 2 slots per decode CTA (or CTA pair), each
+//   [256, 8448)         split-K arrival counters of the 16-head kernel, 2 per CTA pair
+//                       (each returns to zero when its row is merged)
+//   [8448, ...)         split-K partials: 2 slots per decode CTA (or CTA pair), each
 //                       sized for the widest head group (64 heads)
+constexpr size_t kCountersOff = 256;
+constexpr size_t kPartsOff = 8448;
+constexpr int kMaxPairs = (int)((kPartsOff - kCountersOff) / 8);
+
 struct WsLayout {
   size_t parts_off, total;
 };
 
 WsLayout ws_layout(int sms) {
   WsLayout w;
-  w.parts_off = 256;
+  w.parts_off = kPartsOff;
   w.total = align_up(w.parts_off + (size_t)(2 * sms) * (size_t)Cfg<64>::SLOT_FLOATS * 4, 256);
   return w;
 }
@@ -929,23 +940,38 @@ int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
   return r == CUDA_SUCCESS ? DSA_OK : DSA_ERR_DRIVER;
 }
 
-// The split-K merge for a decode grid of `grid` CTAs (or pairs), launched with
-// programmatic stream serialization so that its launch overlaps the decode's tail.
+// Every kernel of a call is launched with programmatic stream serialization: it may be
+// scheduled while the grid before it drains, runs its set-up, and waits for that grid
+// (griddepcontrol.wait) before it touches global memory.
+cudaLaunchAttribute g_pdl_attr = [] {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}();
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1] = {g_pdl_attr};
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess
+             ? DSA_OK
+             : DSA_ERR_CUDA;
+}
+
+// The split-K merge for a decode grid of `grid` CTAs.
 template <int NHC>
 int launch_merge(const Params& prm, int grid, cudaStream_t stream) {
   if (grid <= 1) return DSA_OK;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(grid - 1), NHC / 16, 1);
-  cfg.blockDim = dim3(kDCkv, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, dsa_merge_kernel<NHC>, prm, grid) == cudaSuccess ? DSA_OK
-                                                                                   : DSA_ERR_CUDA;
+  return launch_pdl(dsa_merge_kernel<NHC>, dim3((unsigned)(grid - 1), NHC / 16, 1),
+                    dim3(kDCkv, 1, 1), 0, stream, prm, grid);
 }
 
 template <int NHC>
@@ -968,8 +994,9 @@ int launch(const CUtensorMap& ckv, const CUtensorMap& kpe, const CUtensorMap& qn
       g_dev[dev].attr_done[ai] = true;
     }
   }
-  dsa_decode_kernel<NHC><<<grid, kThreads, C::SMEM_BYTES, stream>>>(ckv, kpe, qn, qp, prm);
-  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  int rc = launch_pdl(dsa_decode_kernel<NHC>, dim3((unsigned)grid), dim3(kThreads),
+                      (size_t)C::SMEM_BYTES, stream, ckv, kpe, qn, qp, prm);
+  if (rc != DSA_OK) return rc;
   return launch_merge<NHC>(prm, grid, stream);
 }
 
@@ -1038,9 +1065,15 @@ int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
     cap = device_pairs(dev);
     if (cap <= 0) return DSA_ERR_CUDA;
   }
-  pl.grid = (int)(pl.units < cap ? pl.units : cap);
+  // 16 heads: with no more rows than the grid can hold, each row gets a whole CTA pair and
+  // none is split: a split-K merge costs a few dependent global round trips on the tail,
+  // each slow while the other SMs saturate HBM, which outweighs the idle SMs.  Otherwise
+  // (and for the generic kernel) stream-K over the tiles with an equal share per CTA.
+  const int64_t num_rh = a.num_tokens * hg;
+  pl.grid = (int)(pl.pair && num_rh <= cap ? num_rh : (pl.units < cap ? pl.units : cap));
   const size_t slot_bytes = (size_t)(pl.nhc * kDCkv + 2 * pl.nhc) * 4;
-  pl.need = 256 + (size_t)(2 * pl.grid) * slot_bytes;
+  if (pl.pair && pl.grid > kMaxPairs) pl.grid = kMaxPairs;
+  pl.need = kPartsOff + (size_t)(2 * pl.grid) * slot_bytes;
   return DSA_OK;
 }
 
@@ -1092,12 +1125,12 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, int dev, cudaStre
   prm.tpr = pl.tpr;
   prm.scale_log2 = a.sm_scale * kLog2e;
   prm.err = reinterpret_cast<uint32_t*>(ws);
-  prm.parts = reinterpret_cast<float*>(ws + 256);
+  prm.parts = reinterpret_cast<float*>(ws + kPartsOff);
+  prm.counters = reinterpret_cast<uint32_t*>(ws + kCountersOff);
   if (pl.pair) {
-    h16::dsa_decode_h16_kernel<<<2 * pl.grid, h16::kThreads, h16::SMEM_BYTES, st>>>(
-        m_ckv, m_kpe, m_qn, m_qp, prm);
-    if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-    return launch_merge<16>(prm, pl.grid, st);
+    return launch_pdl(h16::dsa_decode_h16_kernel, dim3((unsigned)(2 * pl.grid)),
+                      dim3(h16::kThreads), (size_t)h16::SMEM_BYTES, st, m_ckv, m_kpe, m_qn, m_qp,
+                      prm);
   }
   switch (nhc) {
     case 32: return launch<32>(m_ckv, m_kpe, m_qn, m_qp, prm, pl.grid, dev, st);
@@ -1243,8 +1276,8 @@ extern "C" int dsa_sparse_mla_decode_noalloc(
     scratch = g_noalloc_addr[dev];
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's bytes: the error word must start at zero; the
-  // partials are always written before they are read.
-  if (cudaMemsetAsync(scratch, 0, 4, st) != cudaSuccess) return DSA_ERR_CUDA;
+  // The array keeps the previous call's bytes: the error word and the split-K counters
+  // must start at zero; the partials are always written before they are read.
+  if (cudaMemsetAsync(scratch, 0, kPartsOff, st) != cudaSuccess) return DSA_ERR_CUDA;
   return run_plan(a, pl, static_cast<uint8_t*>(scratch), dev, st);
 }

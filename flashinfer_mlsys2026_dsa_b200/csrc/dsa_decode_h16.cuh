@@ -24,16 +24,17 @@
 //                 issuer those stalls, not the tensor core, set the tile period.
 //   warps 8-15    softmax / epilogue: warp w reads TMEM lanes 32(w%4).. (slots) and
 //                 handles heads 8((w-8)/4) .. +7.
-// The work split (stream-K over (row, 96-slot tile) units per pair), the split-K
-// partial layout and the merge kernel are those of the generic kernel, with a pair in
-// place of a CTA.  Every wait is bounded.
+// The work split is stream-K over (row, 96-slot tile) units per pair, with the generic
+// kernel's split-K partial layout; a row cut between pairs is merged inside this kernel
+// by the pair holding its first tiles (per rank, for its value half), after a bounded
+// wait for the other pairs' partials.  Every wait is bounded.
 #pragma once
 
 namespace dsa {
 namespace h16 {
 
 constexpr int kTS = 96;                  // slots per tile; the score MMA is M=128 and its
-                                         // rows >= kTS read the next 4 KB (never used)
+                                         // rows >= kTS read past the region (never used)
 constexpr int kNH = 16;
 constexpr int kBlk = 4;                  // 64-wide ckv d-blocks per CTA
 constexpr int kRB = kTS * 128;           // one ckv d-block region of a stage
@@ -51,7 +52,8 @@ constexpr int OFF_P = OFF_Q + 2 * kQB;
 constexpr int OFF_X = OFF_P + 2 * kPB;
 constexpr int OFF_BAR = OFF_X + 2 * kXB;
 constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
-constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag
+constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag,
+                                         // [4] unused
 constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][8 heads] floats
 constexpr int SMEM_USED = OFF_RED + 2 * 4 * 8 * 4;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;
@@ -76,17 +78,18 @@ constexpr uint32_t kSw128 = 2, kSw64 = 4;  // UMMA descriptor layout types
 constexpr int kSlotFloats = kNH * kDCkv + 2 * kNH;
 
 enum : int {
-  B_KVF = 0,    // [3] stage landed: one arrive (with its bytes) per producer warp; d-block
-                //     0's warp writes the tile's slot masks before it arrives
-  B_KVE = 3,    // [3][5] d-block region of a stage free again: the kpe region once the
-                //     score has read it, value d-blocks 0-1 / 2-3 once their PV half has
-  B_QF = 18, B_QE = 20,
-  B_SF = 22, B_SE = 24,  // score buffer full / read
-  B_PF = 26, B_PD = 28,  // P written (+ O rescaled) / PV done
-  B_XF = 30,    // [2] the peer's partial scores are in X[b] (st.async complete_tx)
-  B_OF = 32,    // the epilogue has read O
-  B_DRAIN = 33, // [2] used only when an issuer stops early
-  B_COUNT = 35
+  B_KVF = 0,                     // [stage] landed: one arrive (with its bytes) per producer
+                                 // warp; d-block 0's warp writes the slot masks first
+  B_KVE = B_KVF + kStages,       // [stage][5] d-block region free again: the kpe region once
+                                 // the score has read it, value d-blocks 0-1 / 2-3 once
+                                 // their PV half has
+  B_QF = B_KVE + kStages * 5, B_QE = B_QF + 2,
+  B_SF = B_QE + 2, B_SE = B_SF + 2,  // score buffer full / read
+  B_PF = B_SE + 2, B_PD = B_PF + 2,  // P written (+ O rescaled) / PV done
+  B_XF = B_PD + 2,               // [2] the peer's partial scores are in X[b] (complete_tx)
+  B_OF = B_XF + 2,               // the epilogue has read O
+  B_DRAIN = B_OF + 1,            // [2] used only when an issuer stops early
+  B_COUNT = B_DRAIN + 2
 };
 __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * 5 + blk; }
 // X[b] needs no "empty" barrier: the peer writes X[b] for tile i + 2 only after it has
@@ -181,7 +184,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem = misc[0];
-  ptx::launch_dependents();  // the merge grid may be scheduled; it waits for this grid
+  // Launched with programmatic stream serialization: the set-up above overlapped the
+  // previous grid's tail; nothing in global memory is touched before that grid is done.
+  ptx::grid_dep_wait();
+  ptx::launch_dependents();
 
   const int64_t pair = blockIdx.x >> 1;
   const int64_t G = gridDim.x >> 1;
@@ -564,8 +570,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       const int64_t b = s.rh;
       const bool full = (s.t0 == 0 && s.t1 == p.tpr);
-      const int64_t pslot = 2 * pair + (s.rh == first_rh ? 0 : 1);
-      float* part = p.parts + pslot * kSlotFloats;
+      // A row cut between pairs: the pair holding its first tiles (the head, p_lo) ends
+      // its range with them; the others start theirs with the rest and so finish early.
+      // They write their partial and count themselves; the head waits for the count and
+      // merges from its own O in TMEM, so it writes no partial and no fence delays it.
+      const int64_t p_lo = full ? pair : cta_of(b * p.tpr, p.units, G);
+      const int64_t p_hi = full ? pair : cta_of((b + 1) * p.tpr - 1, p.units, G);
+      const bool head = full || pair == p_lo;
+      float* part = p.parts + (2 * pair + (s.rh == first_rh ? 0 : 1)) * kSlotFloats;
+      float o_mine[2][8];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         uint32_t rr[8];
@@ -575,15 +588,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
           const float o = __uint_as_float(rr[h]);
-          const int head = 8 * hh + h;
+          o_mine[mt][h] = o;
+          const int head_idx = 8 * hh + h;
           if (full)
-            p.out[b * p.out_sb + (int64_t)head * p.out_sh + d] =
+            p.out[b * p.out_sb + (int64_t)head_idx * p.out_sh + d] =
                 __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
-          else
-            part[head * kDCkv + d] = o;
+          else if (!head)
+            part[head_idx * kDCkv + d] = o;
         }
       }
-      if (rank == 0 && qd == 0 && lane < 8) {
+      if (qd == 0 && lane < 8) {
         float mh = 0.f, lh = 0.f;  // unrolled select keeps m_run / L in registers
 #pragma unroll
         for (int h = 0; h < 8; ++h)
@@ -591,12 +605,97 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mh = m_run[h];
             lh = L[h];
           }
-        const int head = 8 * hh + lane;
-        if (full)
-          p.lse[b * p.lse_sb + (int64_t)head * p.lse_sh] = lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
-        else {
-          part[kNH * kDCkv + head] = mh;
-          part[kNH * kDCkv + kNH + head] = lh;
+        const int head_idx = 8 * hh + lane;
+        if (full) {
+          if (rank == 0)
+            p.lse[b * p.lse_sb + (int64_t)head_idx * p.lse_sh] =
+                lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+        } else if (!head) {
+          // both ranks write the (identical) scalars, so each rank's merge finds them
+          part[kNH * kDCkv + head_idx] = mh;
+          part[kNH * kDCkv + kNH + head_idx] = lh;
+        }
+      }
+      uint32_t* cnt = p.counters + 2 * p_lo + rank;
+      if (!full && !head) {
+        __threadfence();
+        ptx::bar_sync(kNamedBar, kSmThreads);
+        if (warp == kSm0 && lane == 0) atomicAdd(cnt, 1u);
+      } else if (!full) {
+        if (warp == kSm0 && lane == 0) {
+          // Bounded wait for the other parts of the row (all pairs are co-resident).
+          const uint32_t want = (uint32_t)(p_hi - p_lo);
+          const uint64_t t0 = ptx::cycles();
+          uint32_t got = *reinterpret_cast<volatile uint32_t*>(cnt);
+          while (got != want) {
+            if (ptx::cycles() - t0 > kWaitCycles || misc[2]) {
+              misc[2] = 1;
+              atomicOr(p.err, (uint32_t)DSA_DEVERR_TIMEOUT);
+              break;
+            }
+            __nanosleep(64);
+            got = *reinterpret_cast<volatile uint32_t*>(cnt);
+          }
+          __threadfence();
+          atomicExch(cnt, 0u);  // ready for the next call
+        }
+        ptx::bar_sync(kNamedBar, kSmThreads);
+        __threadfence();
+        float M[8], Lt[8], acc[2][8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          M[h] = m_run[h];
+          Lt[h] = L[h];
+          acc[0][h] = o_mine[0][h];
+          acc[1][h] = o_mine[1][h];
+        }
+        for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
+          // a later pair's range starts inside this row: its partial is in its slot 0
+          const float* pp = p.parts + (2 * cc) * kSlotFloats;
+          float pm[8], pl[8], po[2][8];
+          // every load of the part first, so that the part costs one L2 round trip
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const int head_idx = 8 * hh + h;
+            pm[h] = __ldcg(pp + kNH * kDCkv + head_idx);
+            pl[h] = __ldcg(pp + kNH * kDCkv + kNH + head_idx);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+              po[mt][h] = __ldcg(pp + head_idx * kDCkv + (int)(256 * rank) + 128 * mt + 32 * qd + lane);
+          }
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            // A part with l == 0 saw only padding; its O (maybe stale) is not used.
+            const bool live = pl[h] > 0.f;
+            const bool have = Lt[h] > 0.f;
+            const float mn = !live ? M[h] : (!have ? pm[h] : fmaxf(M[h], pm[h]));
+            const float keep = have ? ptx::ex2(M[h] - mn) : 0.f;
+            const float w = live ? ptx::ex2(pm[h] - mn) : 0.f;
+            Lt[h] = (have ? Lt[h] * keep : 0.f) + (live ? w * pl[h] : 0.f);
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+              acc[mt][h] = (have ? acc[mt][h] * keep : 0.f) + (live ? w * po[mt][h] : 0.f);
+            M[h] = mn;
+          }
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
+#pragma unroll
+          for (int h = 0; h < 8; ++h)
+            p.out[b * p.out_sb + (int64_t)(8 * hh + h) * p.out_sh + d] =
+                __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
+        }
+        if (rank == 0 && qd == 0 && lane < 8) {
+          float mh = 0.f, lh = 0.f;
+#pragma unroll
+          for (int h = 0; h < 8; ++h)
+            if (h == lane) {
+              mh = M[h];
+              lh = Lt[h];
+            }
+          p.lse[b * p.lse_sb + (int64_t)(8 * hh + lane) * p.lse_sh] =
+              lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         }
       }
       ptx::tc_fence_before();

@@ -126,15 +126,16 @@ int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream)
  * nothing (no cudaMalloc, cudaFree or allocating library routine).
  *   - The first call on a device resolves the array's device address (once per device,
  *     with that device current) and keeps it for later calls.
- *   - Limit: the split-K partials must fit in the array: 256 B + 2 x G x slot, where G
+ *   - Limit: the split-K partials must fit in the array: 8448 B + 2 x G x slot, where G
  *     is the call's persistent grid (CTA pairs for num_heads 16, at most 74 on a
  *     148-SM B200; CTAs otherwise, at most the SM count) and slot is 32,896 B for 16
  *     heads, 65,664 B for 32 and 131,328 B for 64 or 128.  num_heads 16 always fits
  *     (4.9 MB); 32 fits up to G = 127 and 64/128 up to G = 63 (small batches).  Beyond
  *     that the call returns DSA_ERR_SCRATCH_LIMIT; use dsa_sparse_mla_decode.
  *   - Every call on a device shares the array and finds the previous call's bytes there:
- *     the call clears the error word it uses (device error bits are not reported by this
- *     entry point) and always writes the partials before reading them.  Calls that
+ *     the call clears the first 8448 bytes (error word and split-K arrival counters;
+ *     device error bits are not reported by this entry point) and always writes the
+ *     partials before reading them.  Calls that
  *     overlap on the GPU (different streams, or concurrent host threads) race on the
  *     array; order them on one stream.
  */
