@@ -252,39 +252,84 @@ def run_ours(args):
     err = read_device_errors(dev)
 
     # ---------------- end to end through the public API, host buffers
-    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-    host_in = [(pin(w.q_nope), pin(w.q_pe), pin(w.sparse_indices)) for w in sets]
-    dev_in = [(torch.empty_like(w.q_nope), torch.empty_like(w.q_pe),
-               torch.empty_like(w.sparse_indices)) for w in sets]
-    host_out = torch.empty(B, H, 512, dtype=torch.bfloat16).pin_memory()
-    host_lse = torch.empty(B, H, dtype=torch.float32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host_in[0])
-    d2h = host_out.numel() * 2 + host_lse.numel() * 4
+    # Every step copies its query and index rows from pinned host memory, runs the public
+    # kernel() and copies out/lse back.  Steps are pipelined the way a server runs them:
+    # host-to-device copies, decode and device-to-host copies go on three streams, with
+    # two device buffer slots, so step k's copies overlap the decode of step k-1.
+    # A step's inputs (q_nope, q_pe, indices) sit in one pinned host buffer and cross in
+    # one copy; out and lse sit in one device buffer and come back in one copy.
+    def packed(parts, device=None, pinned=False):
+        sizes = [t.numel() * t.element_size() for t in parts]
+        offs = [0]
+        for n in sizes[:-1]:
+            offs.append(offs[-1] + (n + 255) // 256 * 256)
+        buf = torch.empty(offs[-1] + sizes[-1], dtype=torch.uint8, device=device,
+                          pin_memory=pinned)
+        views = [buf[o:o + n].view(t.dtype).view(t.shape) for o, n, t in zip(offs, sizes, parts)]
+        return buf, views
+
+    host_in = []
+    for w in sets:
+        buf, views = packed([w.q_nope, w.q_pe, w.sparse_indices], pinned=True)
+        for v, t in zip(views, (w.q_nope, w.q_pe, w.sparse_indices)):
+            v.copy_(t.cpu())
+        host_in.append(buf)
+    NSLOT = 2
+    dev_in = [packed([sets[0].q_nope, sets[0].q_pe, sets[0].sparse_indices], device=dev)
+              for _ in range(NSLOT)]
+    out_proto = [torch.empty(B, H, 512, dtype=torch.bfloat16), torch.empty(B, H, dtype=torch.float32)]
+    dev_out = [packed(out_proto, device=dev) for _ in range(NSLOT)]
+    host_out = [packed(out_proto, pinned=True) for _ in range(NSLOT)]
+    h2d = host_in[0].numel()
+    d2h = host_out[0][0].numel()
+    s_in, s_run, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_done = [ev() for _ in range(NSLOT)]
+    run_done = [ev() for _ in range(NSLOT)]
+    out_done = [ev() for _ in range(NSLOT)]
+    started = [False] * NSLOT
+    home = torch.cuda.current_stream(dev)
 
     def e2e_step(k):
         w = sets[k % N_SETS]
-        qn, qp, idx = dev_in[k % N_SETS]
-        hq, hp, hi = host_in[k % N_SETS]
-        qn.copy_(hq, non_blocking=True)
-        qp.copy_(hp, non_blocking=True)
-        idx.copy_(hi, non_blocking=True)
-        kernel(qn, qp, w.ckv_cache, w.kpe_cache, idx, w.sm_scale, out, lse)
-        host_out.copy_(out, non_blocking=True)
-        host_lse.copy_(lse, non_blocking=True)
+        sl = k % NSLOT
+        ibuf, (qn, qp, idx) = dev_in[sl]
+        obuf, (o, l) = dev_out[sl]
+        torch.cuda.set_stream(s_in)
+        if started[sl]:
+            s_in.wait_event(run_done[sl])          # the decode of step k-2 read this slot
+        ibuf.copy_(host_in[k % N_SETS], non_blocking=True)
+        in_done[sl].record(s_in)
+        torch.cuda.set_stream(s_run)
+        s_run.wait_event(in_done[sl])
+        if started[sl]:
+            s_run.wait_event(out_done[sl])         # step k-2's outputs have been copied out
+        kernel(qn, qp, w.ckv_cache, w.kpe_cache, idx, w.sm_scale, o, l)
+        run_done[sl].record(s_run)
+        torch.cuda.set_stream(s_out)
+        s_out.wait_event(run_done[sl])
+        host_out[sl][0].copy_(obuf, non_blocking=True)
+        out_done[sl].record(s_out)
+        torch.cuda.set_stream(home)
+        started[sl] = True
 
-    with torch.cuda.stream(stream):
-        for k in range(max(3, args.warmup)):
-            e2e_step(k)
-        stream.synchronize()
-        barrier()
-        f0 = torch.cuda.Event(enable_timing=True)
-        f1 = torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for k in range(steps):
-            e2e_step(k)
-        f1.record(stream)
-        stream.synchronize()
+    for k in range(max(3, args.warmup)):
+        e2e_step(k)
+    torch.cuda.synchronize(dev)
+    barrier()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(s_in)
+    s_run.wait_event(f0)
+    s_out.wait_event(f0)
+    for k in range(steps):
+        e2e_step(k)
+    s_in.wait_event(out_done[(steps - 1) % NSLOT])
+    f1.record(s_in)
+    f1.synchronize()
     e2e_ms = f0.elapsed_time(f1)
+    # the last step's results really are on the host
+    assert torch.isfinite(host_out[(steps - 1) % NSLOT][1][1]).any()
 
     dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_ms], world, dev)
     ms_per_step = dev_ms / steps
@@ -321,7 +366,11 @@ def run_ours(args):
                      "traffic": None, "peak_source": peak_kind,
                      "algorithmic_bytes_per_call": int(bytes_per_step)},
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 4)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 4),
+                "method": "public kernel() per step; one pinned H2D copy of the step's q_nope, "
+                          "q_pe, indices and one D2H copy of its out, lse inside the timed "
+                          "region; copies and decode on three streams with two buffer slots "
+                          "(step k's copies overlap step k-1's decode)"},
         "gpu_launches": 2 * steps,
         "clocks": clk.summary(),
         "device_errors": err,

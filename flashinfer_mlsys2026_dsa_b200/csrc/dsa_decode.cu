@@ -929,15 +929,56 @@ WsLayout ws_layout(int sms) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Encoded tensor maps of recent calls (per host thread): a decode loop reuses its pools and
+// usually its query buffers, and encoding costs microseconds of host time per map.
+struct MapKey {
+  const void* base;
+  int rank;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  int swz;
+  bool operator==(const MapKey& o) const { return memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapCache {
+  static constexpr int kWays = 16;
+  MapKey key[kWays];
+  CUtensorMap map[kWays];
+  bool used[kWays] = {};
+  int next = 0;
+};
+thread_local MapCache t_maps;
+
 int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
            const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  MapKey k;
+  memset(&k, 0, sizeof(k));  // padding bytes take part in the comparison
+  k.base = base;
+  k.rank = rank;
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) k.strides[i] = strides_bytes[i];
+  k.swz = (int)swz;
+  MapCache& c = t_maps;
+  for (int w = 0; w < MapCache::kWays; ++w)
+    if (c.used[w] && c.key[w] == k) {
+      *m = c.map[w];
+      return DSA_OK;
+    }
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return DSA_ERR_DRIVER;
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
                   dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? DSA_OK : DSA_ERR_DRIVER;
+  if (r != CUDA_SUCCESS) return DSA_ERR_DRIVER;
+  const int w = c.next;
+  c.next = (c.next + 1) % MapCache::kWays;
+  c.key[w] = k;
+  c.map[w] = *m;
+  c.used[w] = true;
+  return DSA_OK;
 }
 
 // Every kernel of a call is launched with programmatic stream serialization: it may be

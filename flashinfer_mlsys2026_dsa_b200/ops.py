@@ -40,12 +40,15 @@ def _check(code: int, what: str) -> None:
 def workspace_for(device: torch.device, stream_handle: int, num_tokens: int, num_heads: int,
                   topk: int) -> torch.Tensor:
     """The cached, zero-initialised workspace of (device, stream), grown on demand."""
+    key = (device.index or 0, stream_handle)
+    ws = _workspaces.get(key)
+    if ws is not None:
+        return ws  # its size depends only on the device
     lib = _native.load()
     need = int(lib.dsa_sparse_mla_decode_workspace_size(num_tokens, num_heads, topk,
                                                         device.index or 0))
     if need == 0:
         raise ValueError(f"unsupported problem: num_heads={num_heads}, topk={topk}")
-    key = (device.index or 0, stream_handle)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < need:
@@ -54,37 +57,42 @@ def workspace_for(device: torch.device, stream_handle: int, num_tokens: int, num
     return ws
 
 
+_BF16 = torch.bfloat16
+
+
 def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
-    tensors = dict(q_nope=q_nope, q_pe=q_pe, ckv_cache=ckv_cache, kpe_cache=kpe_cache,
-                   sparse_indices=sparse_indices, output=output, lse=lse)
-    for name, t in tensors.items():
+    tensors = (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache),
+               ("kpe_cache", kpe_cache), ("sparse_indices", sparse_indices), ("output", output),
+               ("lse", lse))
+    for name, t in tensors:
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
         if not t.is_cuda:
             raise ValueError(f"{name} must be a CUDA tensor (this operator has no CPU path)")
     dev = q_nope.device
-    for name, t in tensors.items():
+    for name, t in tensors[1:]:
         if t.device != dev:
             raise ValueError(f"{name} is on {t.device}, expected {dev}")
-    for name in ("q_nope", "q_pe", "ckv_cache", "kpe_cache", "output"):
-        if tensors[name].dtype != torch.bfloat16:
-            raise TypeError(f"{name} must be bfloat16, got {tensors[name].dtype}")
+    for name, t in tensors[:4] + tensors[5:6]:
+        if t.dtype != _BF16:
+            raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
     if sparse_indices.dtype != torch.int32:
         raise TypeError(f"sparse_indices must be int32, got {sparse_indices.dtype}")
     if lse.dtype != torch.float32:
         raise TypeError(f"lse must be float32, got {lse.dtype}")
-    if q_nope.dim() != 3 or q_nope.shape[-1] != D_CKV:
-        raise ValueError(f"q_nope must be [num_tokens, num_heads, {D_CKV}], got {tuple(q_nope.shape)}")
-    B, H, _ = q_nope.shape
-    if tuple(q_pe.shape) != (B, H, D_KPE):
+    qs = q_nope.shape
+    if len(qs) != 3 or qs[2] != D_CKV:
+        raise ValueError(f"q_nope must be [num_tokens, num_heads, {D_CKV}], got {tuple(qs)}")
+    B, H = qs[0], qs[1]
+    if q_pe.shape != (B, H, D_KPE):
         raise ValueError(f"q_pe must be [{B}, {H}, {D_KPE}], got {tuple(q_pe.shape)}")
     if ckv_cache.shape[-1] != D_CKV or kpe_cache.shape[-1] != D_KPE:
         raise ValueError("ckv_cache / kpe_cache last dims must be 512 / 64")
     if sparse_indices.dim() != 2 or sparse_indices.shape[0] != B:
         raise ValueError(f"sparse_indices must be [{B}, topk], got {tuple(sparse_indices.shape)}")
-    if tuple(output.shape) != (B, H, D_CKV):
+    if output.shape != (B, H, D_CKV):
         raise ValueError(f"output must be [{B}, {H}, {D_CKV}], got {tuple(output.shape)}")
-    if tuple(lse.shape) != (B, H):
+    if lse.shape != (B, H):
         raise ValueError(f"lse must be [{B}, {H}], got {tuple(lse.shape)}")
     if H not in SUPPORTED_HEADS:
         raise ValueError(f"num_heads={H} is not supported (supported: {SUPPORTED_HEADS})")
@@ -108,7 +116,7 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
     and does not synchronise.
     """
     _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
-    lib = _native.load()
+    lib = _native._lib or _native.load()
     B, H, _ = q_nope.shape
     topk = sparse_indices.shape[1]
     if B == 0:
@@ -124,8 +132,9 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
     if ckv.shape[0] != kpe.shape[0]:
         raise ValueError("ckv_cache and kpe_cache hold different slot counts")
     out_t = output if output.stride(-1) == 1 else torch.empty_like(output, memory_format=torch.contiguous_format)
-    stream = torch.cuda.current_stream(q_nope.device)
-    ws = workspace_for(q_nope.device, stream.cuda_stream, B, H, topk)
+    dev_index = q_nope.get_device()
+    stream = torch._C._cuda_getCurrentRawStream(dev_index)
+    ws = workspace_for(q_nope.device, stream, B, H, topk)
     rc = lib.dsa_sparse_mla_decode(
         q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
         q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
@@ -135,7 +144,7 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
         float(sm_scale),
         out_t.data_ptr(), out_t.stride(0), out_t.stride(1),
         lse.data_ptr(), lse.stride(0), lse.stride(1),
-        B, H, topk, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        B, H, topk, ws.data_ptr(), ws.numel(), stream)
     _check(rc, "dsa_sparse_mla_decode")
     if out_t is not output:
         output.copy_(out_t)
