@@ -174,6 +174,11 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (read + write) of one decode launch, from the ncu capture summarised in
+# profiles/dsa_decode_h16_b64_h16_metrics.md (dram__bytes_read.sum + dram__bytes_write.sum).
+MEASURED_TRAFFIC = {"b64_h16": 162413824}
+
+
 def max_over_ranks(values, world, device):
     """Element-wise max of per-rank timings (ms) over all ranks of the default group."""
     import torch
@@ -212,6 +217,9 @@ def run_ours(args):
     sets = [workloads.make(args.workload, device=dev, seed=args.seed * 97 + s, rank=rank,
                            world_size=wl_world) for s in range(N_SETS)]
     B, H = sets[0].num_tokens, sets[0].num_heads
+    # kernels of this library per call: the 16-head cluster kernel merges split rows itself;
+    # the generic kernel is followed by its split-K merge kernel
+    launches_per_call = 1 if H == 16 else 2
     bytes_per_step = sum(w.algorithmic_bytes() for w in sets) / N_SETS
     out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, H, dtype=torch.float32, device=dev)
@@ -363,7 +371,7 @@ def run_ours(args):
                          f"(> 126 MB L2)", "timing": "CUDA graph replay, CUDA events"},
         "roofline": {"bound": "hbm", "achieved": round(per_call_gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(per_call_gbs / peak, 4),
-                     "traffic": None, "peak_source": peak_kind,
+                     "traffic": MEASURED_TRAFFIC.get(args.workload), "peak_source": peak_kind,
                      "algorithmic_bytes_per_call": int(bytes_per_step)},
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 4),
@@ -371,7 +379,7 @@ def run_ours(args):
                           "q_pe, indices and one D2H copy of its out, lse inside the timed "
                           "region; copies and decode on three streams with two buffer slots "
                           "(step k's copies overlap step k-1's decode)"},
-        "gpu_launches": 2 * steps,
+        "gpu_launches": steps * launches_per_call,
         "clocks": clk.summary(),
         "device_errors": err,
     }
