@@ -1,4 +1,6 @@
-// DSA decode for 16 heads (one head group): a two-CTA cluster per pair of SMs.
+// DSA decode on two-CTA clusters, one 16-head group per work unit (H = 16, 32, 64 or 128:
+// a row with H heads is H/16 units that gather the same slots; the re-gathers of a row's
+// other groups mostly hit L2).
 //
 // Why a pair: with 16 heads the score MMA is S^T[slots x 16] = K . Q^T, whose cost is
 // set by the number of MMA instructions (an M=128, N=16 MMA costs about as much as an
@@ -112,11 +114,10 @@ __device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t 
          ((uint64_t)layout << 61);
 }
 
-__device__ __forceinline__ void slot_ids(const Params& p, int64_t uu, bool has, int g,
+// Slot ids of tile t of (row, 16-head group) rh for a producer lane's group g; -1 past topk.
+__device__ __forceinline__ void slot_ids(const Params& p, int64_t rh, int t, bool has, int g,
                                          int (&r)[4]) {
-  const int64_t row = uu / p.tpr;
-  const int t = (int)(uu % p.tpr);
-  const int32_t* ir = p.idx + row * p.idx_sb;
+  const int32_t* ir = p.idx + (rh >> p.hg_shift) * p.idx_sb;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int k = t * kTS + 4 * g + e;
@@ -207,11 +208,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!wait(bar(B_QE + qb), (uint32_t)(((seg >> 1) & 1) ^ 1))) break;
         ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)kQB);
         const uint32_t qd = sbase + (uint32_t)(OFF_Q + qb * kQB);
-        const int b = (int)s.rh;
+        const int b = (int)(s.rh >> p.hg_shift);
+        const int h0 = kNH * (int)(s.rh & ((1 << p.hg_shift) - 1));
         for (int j = 0; j < kBlk; ++j)
-          ptx::tma_load_3d(qd + (uint32_t)(j * 2048), &tm_qn, (int)(256 * rank) + 64 * j, 0, b,
+          ptx::tma_load_3d(qd + (uint32_t)(j * 2048), &tm_qn, (int)(256 * rank) + 64 * j, h0, b,
                            bar(B_QF + qb));
-        ptx::tma_load_3d(qd + (uint32_t)(kBlk * 2048), &tm_qp, (int)(32 * rank), 0, b,
+        ptx::tma_load_3d(qd + (uint32_t)(kBlk * 2048), &tm_qp, (int)(32 * rank), h0, b,
                          bar(B_QF + qb));
         ++seg;
       }
@@ -237,10 +239,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
     int64_t n_issued = 0;
     int cur[4], nxt[4];
-    if (u_lo < u_hi) slot_ids(p, u_lo, has, g, cur);
+    // (rh, t) of the next tile to prefetch ids for, stepped without divisions
+    int64_t n_rh = u_lo / p.tpr;
+    int n_t = (int)(u_lo - n_rh * p.tpr);
+    if (u_lo < u_hi) slot_ids(p, n_rh, n_t, has, g, cur);
+    int st = 0;
+    uint32_t phase = 0;
     for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
-      if (uu + 1 < u_hi) slot_ids(p, uu + 1, has, g, nxt);
-      const int st = (int)(i % kStages);
+      if (++n_t == p.tpr) {
+        n_t = 0;
+        ++n_rh;
+      }
+      if (uu + 1 < u_hi) slot_ids(p, n_rh, n_t, has, g, nxt);
       uint32_t nib = 0;
       bool bad = false;
 #pragma unroll
@@ -260,7 +270,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
       }
       if (lane == 0) {
-        ok = wait(bar(kve(st, blk)), (uint32_t)(((i / kStages) & 1) ^ 1));
+        ok = wait(bar(kve(st, blk)), phase ^ 1u);
         if (ok) {
           if (blk == 0) {
             masks[st * 4 + 0] = w0;
@@ -279,6 +289,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                          make_int4(cur[0], cur[1], cur[2], cur[3]), bar(B_KVF + st), policy);
 #pragma unroll
       for (int e = 0; e < 4; ++e) cur[e] = nxt[e];
+      if (++st == kStages) {
+        st = 0;
+        phase ^= 1u;
+      }
     }
     if (!ok && lane == 0) {
       const Waiter drain{misc + 3, p.err};
@@ -416,7 +430,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool aborted = false;
     int64_t u = u_lo;
     Segment s;
-    const int64_t first_rh = u_lo / p.tpr;
     float m_run[8], l_part[8];
     while (!aborted && next_segment(u, u_hi, p.tpr, s)) {
 #pragma unroll
@@ -568,16 +581,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const float* r4 = red_sum + hh * 32 + h;
         L[h] = (r4[0] + r4[8]) + (r4[16] + r4[24]);
       }
-      const int64_t b = s.rh;
+      const int64_t rh = s.rh;                        // (row, 16-head group)
+      const int64_t b = rh >> p.hg_shift;
+      const int h0 = kNH * (int)(rh & ((1 << p.hg_shift) - 1));   // first head of the group
       const bool full = (s.t0 == 0 && s.t1 == p.tpr);
       // A row cut between pairs: the pair holding its first tiles (the head, p_lo) ends
       // its range with them; the others start theirs with the rest and so finish early.
       // They write their partial and count themselves; the head waits for the count and
       // merges from its own O in TMEM, so it writes no partial and no fence delays it.
-      const int64_t p_lo = full ? pair : cta_of(b * p.tpr, p.units, G);
-      const int64_t p_hi = full ? pair : cta_of((b + 1) * p.tpr - 1, p.units, G);
+      const int64_t p_lo = full ? pair : cta_of(rh * p.tpr, p.units, G);
+      const int64_t p_hi = full ? pair : cta_of((rh + 1) * p.tpr - 1, p.units, G);
       const bool head = full || pair == p_lo;
-      float* part = p.parts + (2 * pair + (s.rh == first_rh ? 0 : 1)) * kSlotFloats;
+      // a pair writes a partial only for the row its range starts inside: one slot each
+      float* part = p.parts + pair * kSlotFloats;
       float o_mine[2][8];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
@@ -591,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           o_mine[mt][h] = o;
           const int head_idx = 8 * hh + h;
           if (full)
-            p.out[b * p.out_sb + (int64_t)head_idx * p.out_sh + d] =
+            p.out[b * p.out_sb + (int64_t)(h0 + head_idx) * p.out_sh + d] =
                 __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
           else if (!head)
             part[head_idx * kDCkv + d] = o;
@@ -608,7 +624,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int head_idx = 8 * hh + lane;
         if (full) {
           if (rank == 0)
-            p.lse[b * p.lse_sb + (int64_t)head_idx * p.lse_sh] =
+            p.lse[b * p.lse_sb + (int64_t)(h0 + head_idx) * p.lse_sh] =
                 lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         } else if (!head) {
           // both ranks write the (identical) scalars, so each rank's merge finds them
@@ -650,8 +666,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           acc[1][h] = o_mine[1][h];
         }
         for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
-          // a later pair's range starts inside this row: its partial is in its slot 0
-          const float* pp = p.parts + (2 * cc) * kSlotFloats;
+          // a later pair's range starts inside this row: its partial is in its slot
+          const float* pp = p.parts + cc * kSlotFloats;
           float pm[8], pl[8], po[2][8];
           // every load of the part first, so that the part costs one L2 round trip
 #pragma unroll
@@ -683,7 +699,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
 #pragma unroll
           for (int h = 0; h < 8; ++h)
-            p.out[b * p.out_sb + (int64_t)(8 * hh + h) * p.out_sh + d] =
+            p.out[b * p.out_sb + (int64_t)(h0 + 8 * hh + h) * p.out_sh + d] =
                 __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
         }
         if (rank == 0 && qd == 0 && lane < 8) {
@@ -694,7 +710,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               mh = M[h];
               lh = Lt[h];
             }
-          p.lse[b * p.lse_sb + (int64_t)(8 * hh + lane) * p.lse_sh] =
+          p.lse[b * p.lse_sb + (int64_t)(h0 + 8 * hh + lane) * p.lse_sh] =
               lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         }
       }

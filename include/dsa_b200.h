@@ -121,17 +121,17 @@ int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream)
  * the caller's workspace.
  *
  * Arguments are those of dsa_sparse_mla_decode() without the workspace.  Instead of a
- * workspace the call uses a fixed 16 MiB array that the library's CUDA module holds on
+ * workspace the call uses a fixed 2 MiB array that the library's CUDA module holds on
  * every device that loads it, until the process exits; the call itself allocates
  * nothing (no cudaMalloc, cudaFree or allocating library routine).
  *   - The first call on a device resolves the array's device address (once per device,
  *     with that device current) and keeps it for later calls.
- *   - Limit: the split-K partials must fit in the array: 8448 B + 2 x G x slot, where G
- *     is the call's persistent grid (CTA pairs for num_heads 16, at most 74 on a
- *     148-SM B200; CTAs otherwise, at most the SM count) and slot is 32,896 B for 16
- *     heads, 65,664 B for 32 and 131,328 B for 64 or 128.  num_heads 16 always fits
- *     (4.9 MB); 32 fits up to G = 127 and 64/128 up to G = 63 (small batches).  Beyond
- *     that the call returns DSA_ERR_SCRATCH_LIMIT; use dsa_sparse_mla_decode.
+ *   - Limit: 8448 bytes of header and split-K counters, plus 32,896 bytes per cluster
+ *     pair of the persistent grid when rows are split between pairs.  A call whose
+ *     (row, 16-head group) count fits the grid (at most 74 on a 148-SM B200, e.g. 64
+ *     rows of 16 heads) splits no row and always fits; a larger call runs split rows on
+ *     every pair and needs 2.4 MB, beyond the array: it returns DSA_ERR_SCRATCH_LIMIT
+ *     (use dsa_sparse_mla_decode).
  *   - Every call on a device shares the array and finds the previous call's bytes there:
  *     the call clears the first 8448 bytes (error word and split-K arrival counters;
  *     device error bits are not reported by this entry point) and always writes the
