@@ -46,12 +46,14 @@ constexpr int kStages = 3;
 constexpr int kGroups = kTS / 4;         // gather4 copies per d-block per tile
 constexpr int kPVKs = kTS / 16;          // K steps of one PV MMA chain
 constexpr int kQB = kBlk * 2048 + 1024;  // one Q buffer: 4 x [16 x 64] SW128 + [16 x 32] SW64
-constexpr int kPB = 4096;                // P^T [16 x 128 slots] bf16, SW128 K-major
+constexpr int kPB = 4096;                // P^T [16 x 128 slots] bf16, SW128 K-major; one
+                                         // per stage: stage s is refilled only after the PV
+                                         // that read P[s] completed, so P[s] is then free
 constexpr int kXB = kTS * kNH * 4;       // partial scores from the peer, fp32 [kTS][16]
 constexpr int OFF_KV = 0;
 constexpr int OFF_Q = kStages * kStageB;
 constexpr int OFF_P = OFF_Q + 2 * kQB;
-constexpr int OFF_X = OFF_P + 2 * kPB;
+constexpr int OFF_X = OFF_P + kStages * kPB;
 constexpr int OFF_BAR = OFF_X + 2 * kXB;
 constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
 constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag,
@@ -233,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t dst_off =
         is_kpe ? (uint32_t)(kBlk * kRB + g * 256) : (uint32_t)(blk * kRB + g * 512);
     const int col = is_kpe ? (int)(32 * rank) : (int)(256 * rank) + 64 * blk;
-    const uint32_t tile_bytes = (uint32_t)kGroups * (is_kpe ? 256u : 512u);
+    const uint32_t req_bytes = is_kpe ? 256u : 512u;
     const CUtensorMap* map = is_kpe ? &tm_kpe : &tm_ckv;
     const uint64_t policy = ptx::policy_evict_first();
     bool ok = true;
@@ -261,6 +263,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         nib |= (cur[e] >= 0 ? 1u : 0u) << e;
       }
+      // A group of four padding slots is not requested at all (its value rows are
+      // cleared by the softmax warps, its scores masked).
+      const bool issue = nib != 0u;
+      const uint32_t n_req = (uint32_t)__popc(__ballot_sync(0xffffffffu, issue));
       uint32_t w0 = 0, w1 = 0, w2 = 0;
       if (blk == 0) {
         if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
@@ -278,13 +284,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             masks[st * 4 + 2] = w2;
             masks[st * 4 + 3] = w0 | w1 | w2;  // nonzero: the tile has a valid slot
           }
-          ptx::mbar_arrive_expect_tx(bar(B_KVF + st), tile_bytes);
+          ptx::mbar_arrive_expect_tx(bar(B_KVF + st), n_req * req_bytes);
         }
       }
       ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
       if (!ok) break;
       n_issued = i + 1;
-      if (has)
+      if (issue)
         ptx::tma_gather4(sbase + (uint32_t)(OFF_KV + st * kStageB) + dst_off, map, col,
                          make_int4(cur[0], cur[1], cur[2], cur[3]), bar(B_KVF + st), policy);
 #pragma unroll
@@ -386,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (masks[st * 4 + 3] != 0u) {
             ptx::tc_fence_after();
             const uint64_t vo = (uint64_t)((st * kStageB) >> 4);
-            const uint64_t po = (uint64_t)(((int)(j & 1) * kPB) >> 4);
+            const uint64_t po = (uint64_t)((st * kPB) >> 4);
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
@@ -527,11 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         if (aborted) continue;  // the next vote ends the loop for every thread
-        if (i >= 2 && !wait(bar(B_PD + (int)(i & 1)), (uint32_t)(((i - 2) >> 1) & 1))) {
-          aborted = true;
-          continue;
-        }
-        uint8_t* pbuf = sgen + OFF_P + (int)(i & 1) * kPB + (slot >> 6) * 2048;
+        uint8_t* pbuf = sgen + OFF_P + st * kPB + (slot >> 6) * 2048;
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
           const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
