@@ -57,7 +57,7 @@ constexpr int OFF_X = OFF_P + kStages * kPB;
 constexpr int OFF_BAR = OFF_X + 2 * kXB;
 constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
 constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag,
-                                         // [4] unused
+                                         // [6] the peer's abort flag (written at exit)
 constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][8 heads] floats
 constexpr int SMEM_USED = OFF_RED + 2 * 4 * 8 * 4;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;
@@ -168,6 +168,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::mbar_init(bar(B_DRAIN + 1), 1);
     misc[2] = 0;
     misc[3] = 0;
+    misc[6] = 0;
     ptx::fence_mbar_init();
     ptx::mbar_arrive_expect_tx(bar(B_XF + 0), (uint32_t)kXB);
     ptx::mbar_arrive_expect_tx(bar(B_XF + 1), (uint32_t)kXB);
@@ -724,8 +725,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  // Neither CTA leaves while the other may still write its exchange buffer.
+  // Neither CTA leaves while the other may still write its exchange buffer.  On the normal
+  // path every partial sent was also received.  After a CTA gave up on a wait, the peer may
+  // have sent partials it never waited for: once both CTAs are past their loops (no more
+  // sends), let those in-flight stores land before either CTA exits.
+  // Each CTA tells the other whether it gave up (both are alive until the first barrier),
+  // so that both take the same exit path.
+  if (threadIdx.x == 0)
+    ptx::st_cluster_u32(ptx::mapa(sbase + (uint32_t)(OFF_MISC + 6 * 4), peer), misc[2]);
   ptx::cluster_sync();
+  if (misc[2] | misc[6]) {
+    if (threadIdx.x == 0) {
+      const uint64_t t0 = ptx::cycles();
+      while (ptx::cycles() - t0 < 200000ull) __nanosleep(256);  // ~0.1 ms >> store latency
+    }
+    __syncthreads();
+    ptx::cluster_sync();
+  }
   if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, (uint32_t)TMEM_COLS);

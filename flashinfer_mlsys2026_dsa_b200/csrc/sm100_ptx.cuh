@@ -193,11 +193,8 @@ __device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
-                                              uint32_t d) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 // Asynchronous 16-byte store into another CTA's shared memory that signals complete_tx
 // (16 bytes) on an mbarrier of that CTA when the data has landed.
@@ -208,24 +205,6 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t a, ui
       "[%5];" ::"r"(remote_addr),
       "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
       : "memory");
-}
-// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior
-// writes (including shared::cluster stores) at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
-               : "memory");
-}
-// try_wait with cluster-scope acquire: what the arriving CTA released becomes visible.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
 }
 // Every thread of every CTA of the cluster.
 __device__ __forceinline__ void cluster_sync() {
