@@ -88,5 +88,35 @@ def load(build_if_missing: bool = True):
         return lib
 
 
+_ext = None
+_ext_tried = False
+
+
+def ext():
+    """The torch binding of the C ABI (built in-tree by ``build.build_ext``), or None.
+
+    It is a faster route to the same native entry point, not a different implementation:
+    when it is missing the ctypes route runs the same CUDA kernel.
+    """
+    global _ext, _ext_tried
+    if _ext_tried:
+        return _ext
+    load()  # the binding links libdsa_b200.so; make sure that is the copy loaded (own lock)
+    with _lock:
+        if not _ext_tried:
+            path = _build.EXT_PATH
+            if os.path.exists(path) and not _build.ext_is_stale():
+                import importlib.machinery
+                import importlib.util
+
+                loader = importlib.machinery.ExtensionFileLoader(_build.EXT_NAME, path)
+                spec = importlib.util.spec_from_file_location(_build.EXT_NAME, path, loader=loader)
+                mod = importlib.util.module_from_spec(spec)
+                loader.exec_module(mod)
+                _ext = mod
+            _ext_tried = True
+    return _ext
+
+
 def status_text(code: int) -> str:
     return load().dsa_status_string(int(code)).decode()

@@ -57,5 +57,34 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
+EXT_NAME = "_dsa_torch"
+EXT_DIR = os.path.join(PKG_DIR, "_ext_build")
+EXT_PATH = os.path.join(EXT_DIR, EXT_NAME + ".so")
+EXT_SOURCES = [os.path.join(CSRC, "torch_binding.cpp")]
+
+
+def ext_is_stale() -> bool:
+    if not os.path.exists(EXT_PATH):
+        return True
+    t = os.path.getmtime(EXT_PATH)
+    deps = EXT_SOURCES + [LIB_PATH, os.path.join(INCLUDE, "dsa_b200.h")]
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> str:
+    """Build the torch binding of the C ABI (a C++ extension linked to libdsa_b200.so)."""
+    if not force and not ext_is_stale():
+        return EXT_PATH
+    from torch.utils import cpp_extension
+    os.makedirs(EXT_DIR, exist_ok=True)
+    cpp_extension.load(name=EXT_NAME, sources=EXT_SOURCES, extra_include_paths=[INCLUDE],
+                       extra_cflags=["-O2"],
+                       extra_ldflags=[f"-L{PKG_DIR}", "-ldsa_b200", f"-Wl,-rpath,{PKG_DIR}"],
+                       build_directory=EXT_DIR, verbose=verbose)
+    os.utime(EXT_PATH)  # mark it newer than its inputs even when ninja had nothing to do
+    return EXT_PATH
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_ext(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -58,6 +58,9 @@ def workspace_for(device: torch.device, stream_handle: int, num_tokens: int, num
 
 
 _BF16 = torch.bfloat16
+# native statuses about the arguments: the general route re-validates and raises the
+# precise TypeError / ValueError (-1: the binding did not handle the argument form)
+_REVALIDATE = (-1, 1, 2)
 
 
 def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
@@ -115,6 +118,20 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
     lse [B,H] fp32 (base-2 log-sum-exp).  Runs on the current CUDA stream
     and does not synchronise.
     """
+    ext = _native._ext if _native._ext_tried else _native.ext()
+    if ext is not None and type(q_nope) is torch.Tensor and q_nope.is_cuda:
+        # Fast route: the binding reads the tensors in C++; -1 means "not the plain form",
+        # and the general route below validates, raises or re-lays-out.
+        dev_index = q_nope.get_device()
+        stream = torch._C._cuda_getCurrentRawStream(dev_index)
+        ws = _workspaces.get((dev_index, stream))
+        if ws is not None and q_nope.shape[0] > 0:
+            rc = ext.decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, float(sm_scale),
+                            output, lse, ws, stream)
+            if rc == _native.DSA_OK:
+                return
+            if rc not in _REVALIDATE:
+                _check(rc, "dsa_sparse_mla_decode")
     _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse)
     lib = _native._lib or _native.load()
     B, H, _ = q_nope.shape

@@ -56,7 +56,7 @@ def _paged_indices(rng, seq_lens, topk, num_pages, pad_short=True, mode="uniform
 
 
 CASES = {
-    # configs[0] of the benchmark spec: the CPU-runnable tiny decode.
+    # the CPU-runnable tiny decode (B=2, H=16, topk=256, 32-page pool)
     "tiny_b2_h16_k256": dict(B=2, H=16, topk=256, pages=32, seq=[1024, 1000], kv_scale=1.0),
     "h16_k2048": dict(B=2, H=16, topk=2048, pages=80, seq=[2500, 2100], kv_scale=0.5),
     "h128_k256": dict(B=2, H=128, topk=256, pages=24, seq=[700, 600], kv_scale=0.5),

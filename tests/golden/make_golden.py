@@ -5,8 +5,8 @@ copied):  python tests/golden/make_golden.py /path/to/reference
 
 For every case of cases.py it imports solution/triton/baseline.py of the
 reference, calls its ``kernel`` on CPU tensors and stores the outputs (bf16
-bits and the base-2 LSE) with a SHA-256 of the inputs.  The GPU box never
-needs the reference: the tests only read the .npz.
+bits and the base-2 LSE) with a SHA-256 of the inputs.  The tests never
+need the reference at run time: they only read the .npz.
 """
 from __future__ import annotations
 

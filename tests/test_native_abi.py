@@ -68,3 +68,11 @@ def test_host_side_validation_needs_no_gpu():
 
 def test_build_is_up_to_date():
     assert not build.is_stale(), "libdsa_b200.so is older than its sources"
+
+
+def test_torch_binding_is_built_and_loads():
+    """The fast host route (C++ binding of the C ABI) is present and up to date."""
+    from flashinfer_mlsys2026_dsa_b200 import _native
+    assert not build.ext_is_stale(), "the torch binding is older than its sources"
+    ext = _native.ext()
+    assert ext is not None and hasattr(ext, "decode")
