@@ -69,6 +69,7 @@ constexpr int kMmaWarp = 6;     // score issuer; also allocates TMEM
 constexpr int kPvWarp = 7;
 constexpr int kSm0 = 8;
 constexpr int kSmThreads = 256;
+constexpr int kSmWarps = kSmThreads / 32;
 constexpr uint32_t kNamedBar = 1;
 // Register split after launch (512 threads x 128 = 65536): warpgroups 0-1 (loader,
 // producers, MMA issuer) drop to kRegsLow, the two softmax warpgroups rise to kRegsHigh.
@@ -156,14 +157,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(B_QF + b), 1);
       ptx::mbar_init(bar(B_QE + b), 1);
       ptx::mbar_init(bar(B_SF + b), 1);
-      ptx::mbar_init(bar(B_SE + b), kSmThreads);
-      ptx::mbar_init(bar(B_PF + b), kSmThreads);
+      ptx::mbar_init(bar(B_SE + b), kSmWarps);  // one arrive per softmax warp
+      ptx::mbar_init(bar(B_PF + b), kSmWarps);
       ptx::mbar_init(bar(B_PD + b), 1);
       // X[b] is full once this CTA armed it (one arrive with the expected bytes) and the
       // peer's st.async bytes landed; the peer's stores may come before the arming.
       ptx::mbar_init(bar(B_XF + b), 1);
     }
-    ptx::mbar_init(bar(B_OF), kSmThreads);
+    ptx::mbar_init(bar(B_OF), kSmWarps);
     ptx::mbar_init(bar(B_DRAIN), 1);
     ptx::mbar_init(bar(B_DRAIN + 1), 1);
     misc[2] = 0;
@@ -458,7 +459,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tmem_ld8(tmem + lane_base + (uint32_t)(S_COL + 16 * sb + 8 * hh), own);
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
-        if (ok) ptx::mbar_arrive(bar(B_SE + sb));
+        // One arrive per warp (a barrier arrive is an atomic on one shared word: 256 of them
+        // would serialise); the warp's lanes agree first.
+        if (__all_sync(0xffffffffu, ok) && lane == 0) ptx::mbar_arrive(bar(B_SE + sb));
         // Swap partial scores with the peer: st.async ours into its X[sb] (completing its
         // B_XF[sb] by bytes), then wait for its bytes in ours.
         if (ok && slot_ok) {
@@ -514,7 +517,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             m_run[h] = mn;
           }
           if (o_valid) {
-            if (!wait(bar(B_PD + (int)((i - 1) & 1)), (uint32_t)(((i - 1) >> 1) & 1))) {
+            // the outcome is made warp-uniform: the TMEM loads and stores below are
+            // warp-collective, and a warp continues or stops as one
+            const bool wok = wait(bar(B_PD + (int)((i - 1) & 1)), (uint32_t)(((i - 1) >> 1) & 1));
+            if (!__all_sync(0xffffffffu, wok)) {
               aborted = true;
             } else {
               ptx::tc_fence_after();
@@ -557,7 +563,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         ptx::fence_proxy_async_smem();
         ptx::tc_fence_before();
-        ptx::mbar_arrive(bar(B_PF + (int)(i & 1)));
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(B_PF + (int)(i & 1)));
         o_valid = o_valid || live;
       }
       // ---------------------------------------------------------------- epilogue
@@ -637,29 +644,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       uint32_t* cnt = p.counters + 2 * p_lo + rank;
       if (!full && !head) {
-        __threadfence();
+        // every thread's partial stores, then one release add (cumulative over the barrier)
         ptx::bar_sync(kNamedBar, kSmThreads);
-        if (warp == kSm0 && lane == 0) atomicAdd(cnt, 1u);
+        if (warp == kSm0 && lane == 0) ptx::red_release_gpu_add(cnt, 1u);
       } else if (!full) {
         if (warp == kSm0 && lane == 0) {
-          // Bounded wait for the other parts of the row (all pairs are co-resident).
+          // Bounded wait for the other parts of the row (all pairs are co-resident); the
+          // acquire load orders the partial reads after it (through the barrier below).
           const uint32_t want = (uint32_t)(p_hi - p_lo);
           const uint64_t t0 = ptx::cycles();
-          uint32_t got = *reinterpret_cast<volatile uint32_t*>(cnt);
+          uint32_t got = ptx::ld_acquire_gpu(cnt);
           while (got != want) {
             if (ptx::cycles() - t0 > kWaitCycles || misc[2]) {
               misc[2] = 1;
               atomicOr(p.err, (uint32_t)DSA_DEVERR_TIMEOUT);
               break;
             }
-            __nanosleep(64);
-            got = *reinterpret_cast<volatile uint32_t*>(cnt);
+            __nanosleep(32);
+            got = ptx::ld_acquire_gpu(cnt);
           }
-          __threadfence();
-          atomicExch(cnt, 0u);  // ready for the next call
         }
         ptx::bar_sync(kNamedBar, kSmThreads);
-        __threadfence();
         float M[8], Lt[8], acc[2][8];
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
@@ -716,9 +721,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           p.lse[b * p.lse_sb + (int64_t)(h0 + 8 * hh + lane) * p.lse_sh] =
               lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         }
+        // every part has been counted and read: the counter is ready for the next call
+        if (warp == kSm0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(B_OF));
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(B_OF));
       // The sums are read; the next segment may reuse the slots after its first vote.
     }
   }
