@@ -1,7 +1,7 @@
 /*
  * CPU oracle for the DSA sparse-MLA decode operator.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA path and the
+ * TEST INFRASTRUCTURE ONLY.  This file checks the CUDA path in the tests and is the
  * timed CPU baseline ("port") of bench.py; nothing in the product path links,
  * loads or calls it.  It restates, in plain C, the reference PyTorch
  * implementation `kernel(...)` in solution/triton/baseline.py of

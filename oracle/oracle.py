@@ -1,7 +1,7 @@
 """CPU oracle for the DSA sparse-MLA decode operator (test infrastructure).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import this module.  It is the checker, never the product:
+``bench.py`` may import this module.  It checks the product and is never part of it:
 the product path (``flashinfer_mlsys2026_dsa_b200``) has no CPU fallback and
 never imports it.
 
