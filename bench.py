@@ -199,7 +199,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from flashinfer_mlsys2026_dsa_b200 import kernel, read_device_errors, workloads
+    from flashinfer_mlsys2026_dsa_b200 import kernel, kernel_paged, read_device_errors, workloads
 
     world, rank, local = _dist_setup(args.gpus)
     torch.cuda.set_device(local)
@@ -217,9 +217,8 @@ def run_ours(args):
     sets = [workloads.make(args.workload, device=dev, seed=args.seed * 97 + s, rank=rank,
                            world_size=wl_world) for s in range(N_SETS)]
     B, H = sets[0].num_tokens, sets[0].num_heads
-    # kernels of this library per call: the 16-head cluster kernel merges split rows itself;
-    # the generic kernel is followed by its split-K merge kernel
-    launches_per_call = 1 if H == 16 else 2
+    # kernels of this library per call: one (the cluster kernel merges split rows itself)
+    launches_per_call = 1
     bytes_per_step = sum(w.algorithmic_bytes() for w in sets) / N_SETS
     out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, H, dtype=torch.float32, device=dev)
@@ -258,6 +257,33 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
     dev_ms = e0.elapsed_time(e1)
     err = read_device_errors(dev)
+
+    # ---------------- the same steps through the paged entry (positions + page tables;
+    # the slot ids are formed inside the kernel), device-timed the same way
+    with torch.cuda.stream(stream):
+        pargs = [(w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, w.page_table, w.positions,
+                  w.sm_scale) for w in sets]
+        for a in pargs:
+            kernel_paged(*a, out, lse)
+        stream.synchronize()
+        pgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(pgraph, stream=stream):
+            for a in pargs:
+                kernel_paged(*a, out, lse)
+        for _ in range(max(1, math.ceil(args.warmup / N_SETS))):
+            pgraph.replay()
+        stream.synchronize()
+        barrier()
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        for _ in range(reps):
+            pgraph.replay()
+        p1.record(stream)
+        stream.synchronize()
+    paged_ms = p0.elapsed_time(p1)
+    err |= read_device_errors(dev)
+    del pgraph
 
     # ---------------- end to end through the public API, host buffers
     # Every step copies its query and index rows from pinned host memory, runs the public
@@ -339,7 +365,7 @@ def run_ours(args):
     # the last step's results really are on the host
     assert torch.isfinite(host_out[(steps - 1) % NSLOT][1][1]).any()
 
-    dev_ms, e2e_ms = max_over_ranks([dev_ms, e2e_ms], world, dev)
+    dev_ms, e2e_ms, paged_ms = max_over_ranks([dev_ms, e2e_ms, paged_ms], world, dev)
     ms_per_step = dev_ms / steps
     value, e2e_value = job_gbs(bytes_per_step, steps, world, dev_ms), job_gbs(
         bytes_per_step, steps, world, e2e_ms)
@@ -379,6 +405,11 @@ def run_ours(args):
                           "q_pe, indices and one D2H copy of its out, lse inside the timed "
                           "region; copies and decode on three streams with two buffer slots "
                           "(step k's copies overlap step k-1's decode)"},
+        "paged_entry": {"us_per_call": round(paged_ms / steps * 1e3, 2),
+                        "value": round(job_gbs(bytes_per_step, steps, world, paged_ms), 1),
+                        "unit": "GB/s",
+                        "method": "kernel_paged(): token positions + page tables in, slot ids "
+                                  "formed in the kernel; same steps, bytes and timing as value"},
         "gpu_launches": steps * launches_per_call,
         "clocks": clk.summary(),
         "device_errors": err,

@@ -34,8 +34,16 @@ _DECODE_ARGTYPES = [
     _c.c_void_p,                                    # stream
 ]
 
+# dsa_sparse_mla_decode_paged: the slot ids replaced by page table + positions
+_PAGED_ARGTYPES = (_DECODE_ARGTYPES[:11]
+                   + [_c.c_void_p, _c.c_int64, _c.c_int32, _c.c_int32,  # page_table, stride_b,
+                      #                                                    cols, page_size
+                      _c.c_void_p, _c.c_int64]                          # positions, stride_b
+                   + _DECODE_ARGTYPES[13:])
+
 EXPORTED_SYMBOLS = (
     "dsa_sparse_mla_decode",
+    "dsa_sparse_mla_decode_paged",
     "dsa_sparse_mla_decode_noalloc",
     "dsa_sparse_mla_decode_workspace_size",
     "dsa_read_error_word",
@@ -70,6 +78,8 @@ def load(build_if_missing: bool = True):
             raise NativeLibraryError(f"cannot load {path}: {e}") from e
         lib.dsa_sparse_mla_decode.restype = _c.c_int
         lib.dsa_sparse_mla_decode.argtypes = _DECODE_ARGTYPES
+        lib.dsa_sparse_mla_decode_paged.restype = _c.c_int
+        lib.dsa_sparse_mla_decode_paged.argtypes = _PAGED_ARGTYPES
         lib.dsa_sparse_mla_decode_noalloc.restype = _c.c_int
         lib.dsa_sparse_mla_decode_noalloc.argtypes = _DECODE_ARGTYPES[:-3] + [_c.c_void_p]
         lib.dsa_sparse_mla_decode_workspace_size.restype = _c.c_size_t

@@ -18,6 +18,7 @@ INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libdsa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = [os.path.join(CSRC, "dsa_decode.cu")]
+TVM_BINDING = os.path.join(CSRC, "kernel.cu")
 # every source and header the library is built from (a change to any makes it stale)
 DEPS = sorted(
     [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h"))]
@@ -85,6 +86,49 @@ def build_ext(force: bool = False, verbose: bool = False) -> str:
     return EXT_PATH
 
 
+TVM_NAME = "dsa_tvm_ffi"
+TVM_PATH = os.path.join(EXT_DIR, TVM_NAME + ".so")
+
+
+def tvm_ffi_present() -> bool:
+    try:
+        import tvm_ffi.libinfo  # noqa: F401
+    except ImportError:
+        return False
+    return True
+
+
+def tvm_is_stale() -> bool:
+    if not os.path.exists(TVM_PATH):
+        return True
+    t = os.path.getmtime(TVM_PATH)
+    return any(os.path.getmtime(d) > t for d in DEPS)
+
+
+def build_tvm_ffi(force: bool = False, verbose: bool = False) -> str:
+    """Build the TVM-FFI module (``kernel.cu`` + ``dsa_decode.cu``): the contest's CUDA slot."""
+    if not force and not tvm_is_stale():
+        return TVM_PATH
+    from tvm_ffi import libinfo
+    lib = libinfo.find_libtvm_ffi()
+    os.makedirs(EXT_DIR, exist_ok=True)
+    tmp = TVM_PATH + f".tmp{os.getpid()}"
+    cmd = [nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+           "-Xcompiler", "-fPIC", "-shared", "-cudart", "shared",
+           "-Xlinker", "-rpath,/usr/local/cuda/lib64",
+           "-Xlinker", f"-rpath,{os.path.dirname(lib)}",
+           "-I", INCLUDE, "-I", CSRC, "-I", libinfo.find_include_path(),
+           "-I", libinfo.find_dlpack_include_path(), "-o", tmp, TVM_BINDING, *SOURCES,
+           f"-L{os.path.dirname(lib)}", "-ltvm_ffi"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, TVM_PATH)
+    return TVM_PATH
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
     print(build_ext(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    if tvm_ffi_present():
+        print(build_tvm_ffi(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -46,6 +46,11 @@ struct Params {
   uint32_t* err;
   float* parts;       // split-K partials, one slot per cluster pair
   uint32_t* counters;  // split-K arrival counters, zero between calls
+  // paged calls only: idx holds token positions; page_table rows of pt_cols page ids
+  const int32_t* pt;
+  int64_t pt_sb;
+  int32_t pt_cols;
+  int32_t pg_shift;  // log2(page_size)
 };
 
 // UMMA shared-memory descriptor, 128-byte swizzle, sm_100 (version 1).
@@ -200,22 +205,23 @@ int device_pairs(int dev) {
   if (d.pairs == 0) {
     // The kernel re-splits its register pool per warpgroup (setmaxnreg); refuse a build
     // whose pool is too small for that split, which would stall.
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, h16::dsa_decode_h16_kernel) != cudaSuccess) return 0;
-    if ((int64_t)fa.numRegs * h16::kThreads < 256 * (int64_t)(h16::kRegsLow + h16::kRegsHigh))
-      return 0;
-    if (cudaFuncSetAttribute(h16::dsa_decode_h16_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             h16::SMEM_BYTES) != cudaSuccess)
-      return 0;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (unsigned)(d.sms > 0 ? d.sms : 148), 1, 1);
-    cfg.blockDim = dim3(h16::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = h16::SMEM_BYTES;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, h16::dsa_decode_h16_kernel, &cfg) != cudaSuccess ||
-        n <= 0)
-      return 0;
+    for (auto kern : {h16::dsa_decode_h16_kernel<false>, h16::dsa_decode_h16_kernel<true>}) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+      if ((int64_t)fa.numRegs * h16::kThreads < 256 * (int64_t)(h16::kRegsLow + h16::kRegsHigh))
+        return 0;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               h16::SMEM_BYTES) != cudaSuccess)
+        return 0;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (unsigned)(d.sms > 0 ? d.sms : 148), 1, 1);
+      cfg.blockDim = dim3(h16::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = h16::SMEM_BYTES;
+      int k = 0;
+      if (cudaOccupancyMaxActiveClusters(&k, kern, &cfg) != cudaSuccess || k <= 0) return 0;
+      n = n == 0 ? k : (k < n ? k : n);
+    }
     d.pairs = n;
   }
   return d.pairs;
@@ -350,6 +356,11 @@ struct DecodeArgs {
   int64_t num_tokens;
   int32_t num_heads;
   int32_t topk;
+  // paged calls: idx holds token positions, translated through page_table
+  const int32_t* page_table = nullptr;
+  int64_t pt_sb = 0;
+  int32_t pt_cols = 0;
+  int32_t page_size = 0;
 };
 
 int check_args(const DecodeArgs& a) {
@@ -367,6 +378,12 @@ int check_args(const DecodeArgs& a) {
       (a.qn_sb * 2) % 16 || (a.qn_sh * 2) % 16 || (a.qp_sb * 2) % 16 || (a.qp_sh * 2) % 16 ||
       (a.ckv_ss * 2) % 16 || (a.kpe_ss * 2) % 16)
     return DSA_ERR_MISALIGNED;
+  if (a.page_table != nullptr) {
+    const int32_t ps = a.page_size;
+    if (ps < 1 || ps > (1 << 20) || (ps & (ps - 1)) != 0 || a.pt_cols < 1 ||
+        a.pt_sb < a.pt_cols || (int64_t)a.pt_cols * ps > INT32_MAX)
+      return DSA_ERR_INVALID_ARGUMENT;
+  }
   return DSA_OK;
 }
 
@@ -448,14 +465,34 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   prm.err = reinterpret_cast<uint32_t*>(ws);
   prm.parts = reinterpret_cast<float*>(ws + kPartsOff);
   prm.counters = reinterpret_cast<uint32_t*>(ws + kCountersOff);
-  return launch_pdl(h16::dsa_decode_h16_kernel, dim3((unsigned)(2 * pl.grid)),
-                    dim3(h16::kThreads), (size_t)h16::SMEM_BYTES, st, m_ckv, m_kpe, m_qn, m_qp,
-                    prm);
+  prm.pt = a.page_table;
+  prm.pt_sb = a.pt_sb;
+  prm.pt_cols = a.pt_cols;
+  prm.pg_shift = 0;
+  while (a.page_table != nullptr && (1 << prm.pg_shift) < a.page_size) ++prm.pg_shift;
+  auto kern = a.page_table != nullptr ? h16::dsa_decode_h16_kernel<true>
+                                      : h16::dsa_decode_h16_kernel<false>;
+  return launch_pdl(kern, dim3((unsigned)(2 * pl.grid)), dim3(h16::kThreads),
+                    (size_t)h16::SMEM_BYTES, st, m_ckv, m_kpe, m_qn, m_qp, prm);
 }
 
 int current_device(int& dev) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
   return DSA_OK;
+}
+
+int decode_with_workspace(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  int rc = check_args(a);
+  if (rc != DSA_OK || a.num_tokens == 0) return rc;
+  int dev = 0;
+  if ((rc = current_device(dev)) != DSA_OK) return rc;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return DSA_ERR_CUDA;
+  if (!workspace || workspace_bytes < ws_layout(sms).total) return DSA_ERR_WORKSPACE;
+  Plan pl;
+  if ((rc = make_plan(a, dev, pl)) != DSA_OK) return rc;
+  return run_plan(a, pl, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -506,16 +543,30 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
                      indices_stride_b, sm_scale,       output,          output_stride_b,
                      output_stride_h, lse,             lse_stride_b,    lse_stride_h,
                      num_tokens,      num_heads,       topk};
-  int rc = check_args(a);
-  if (rc != DSA_OK || num_tokens == 0) return rc;
-  int dev = 0;
-  if ((rc = current_device(dev)) != DSA_OK) return rc;
-  const int sms = device_sms(dev);
-  if (sms <= 0) return DSA_ERR_CUDA;
-  if (!workspace || workspace_bytes < ws_layout(sms).total) return DSA_ERR_WORKSPACE;
-  Plan pl;
-  if ((rc = make_plan(a, dev, pl)) != DSA_OK) return rc;
-  return run_plan(a, pl, static_cast<uint8_t*>(workspace), static_cast<cudaStream_t>(stream));
+  return decode_with_workspace(a, workspace, workspace_bytes, stream);
+}
+
+int dsa_sparse_mla_decode_paged(
+    const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h, const void* q_pe,
+    int64_t q_pe_stride_b, int64_t q_pe_stride_h, const void* ckv_cache, int64_t ckv_slot_stride,
+    const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots, const int32_t* page_table,
+    int64_t page_table_stride_b, int32_t page_table_cols, int32_t page_size,
+    const int32_t* positions, int64_t positions_stride_b, float sm_scale, void* output,
+    int64_t output_stride_b, int64_t output_stride_h, float* lse, int64_t lse_stride_b,
+    int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads, int32_t topk, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  if (page_table == nullptr && num_tokens > 0) return DSA_ERR_INVALID_ARGUMENT;
+  DecodeArgs a{q_nope,          q_nope_stride_b, q_nope_stride_h, q_pe,
+               q_pe_stride_b,   q_pe_stride_h,   ckv_cache,       ckv_slot_stride,
+               kpe_cache,       kpe_slot_stride, num_slots,       positions,
+               positions_stride_b, sm_scale,     output,          output_stride_b,
+               output_stride_h, lse,             lse_stride_b,    lse_stride_h,
+               num_tokens,      num_heads,       topk};
+  a.page_table = page_table;
+  a.pt_sb = page_table_stride_b;
+  a.pt_cols = page_table_cols;
+  a.page_size = page_size;
+  return decode_with_workspace(a, workspace, workspace_bytes, stream);
 }
 
 int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word) {

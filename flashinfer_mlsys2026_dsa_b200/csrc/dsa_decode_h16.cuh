@@ -117,9 +117,10 @@ __device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t 
          ((uint64_t)layout << 61);
 }
 
-// Slot ids of tile t of (row, 16-head group) rh for a producer lane's group g; -1 past topk.
-__device__ __forceinline__ void slot_ids(const Params& p, int64_t rh, int t, bool has, int g,
-                                         int (&r)[4]) {
+// Index entries of tile t of (row, 16-head group) rh for a producer lane's group g: slot
+// ids, or token positions in a paged call; -1 past topk.
+__device__ __forceinline__ void tile_entries(const Params& p, int64_t rh, int t, bool has, int g,
+                                             int (&r)[4]) {
   const int32_t* ir = p.idx + (rh >> p.hg_shift) * p.idx_sb;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -128,6 +129,37 @@ __device__ __forceinline__ void slot_ids(const Params& p, int64_t rh, int t, boo
   }
 }
 
+// Slot ids of a paged call's token positions: slot = page_table[row][pos >> pg_shift] *
+// page_size + (pos & (page_size - 1)), the flat slot the pool's [pages, page_size, D] layout
+// gives (fused.py:155-156).  -1 stays padding; a position past the row's table, a negative
+// page or a slot beyond int32 becomes -2, which the producer flags as a bad index.
+__device__ __forceinline__ void translate(const Params& p, int64_t rh, const int (&pos)[4],
+                                          int (&r)[4]) {
+  const int32_t* pr = p.pt + (rh >> p.hg_shift) * p.pt_sb;
+  const int mask = (1 << p.pg_shift) - 1;
+  int page[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int q = pos[e];
+    const bool in_table = q >= 0 && (q >> p.pg_shift) < p.pt_cols;
+    page[e] = in_table ? __ldg(pr + (q >> p.pg_shift)) : (q == -1 ? -1 : -2);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int q = pos[e];
+    if (q < 0 || page[e] < 0) {
+      r[e] = (q == -1) ? -1 : -2;
+    } else {
+      const int64_t slot = ((int64_t)page[e] << p.pg_shift) | (int64_t)(q & mask);
+      r[e] = slot > (int64_t)INT32_MAX ? -2 : (int)slot;
+    }
+  }
+}
+
+// kPaged: sparse_indices holds token positions, translated through the page table by the
+// gather producers (ids are fetched two tiles ahead so the dependent page-table load is off
+// the producer's path).
+template <bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dsa_decode_h16_kernel(const __grid_constant__ CUtensorMap tm_ckv,
                           const __grid_constant__ CUtensorMap tm_kpe,
@@ -242,19 +274,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint64_t policy = ptx::policy_evict_first();
     bool ok = true;
     int64_t n_issued = 0;
-    int cur[4], nxt[4];
-    // (rh, t) of the next tile to prefetch ids for, stepped without divisions
+    int cur[4], nxt[4], ahead[4];
+    // (rh, t) of the tile whose entries are fetched next, stepped without divisions
     int64_t n_rh = u_lo / p.tpr;
     int n_t = (int)(u_lo - n_rh * p.tpr);
-    if (u_lo < u_hi) slot_ids(p, n_rh, n_t, has, g, cur);
-    int st = 0;
-    uint32_t phase = 0;
-    for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
+    int64_t a_rh = n_rh;  // paged: row of the positions held in `ahead`
+    if (u_lo < u_hi) {
+      tile_entries(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
+      if constexpr (kPaged) translate(p, n_rh, ahead, cur);
+    }
+    if constexpr (kPaged) {
       if (++n_t == p.tpr) {
         n_t = 0;
         ++n_rh;
       }
-      if (uu + 1 < u_hi) slot_ids(p, n_rh, n_t, has, g, nxt);
+      a_rh = n_rh;
+      if (u_lo + 1 < u_hi) tile_entries(p, n_rh, n_t, has, g, ahead);
+    }
+    int st = 0;
+    uint32_t phase = 0;
+    for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
+      if constexpr (kPaged) {
+        // slot ids of tile uu + 1 from the positions fetched one tile earlier, then the
+        // positions of tile uu + 2
+        if (uu + 1 < u_hi) translate(p, a_rh, ahead, nxt);
+      }
+      if (++n_t == p.tpr) {
+        n_t = 0;
+        ++n_rh;
+      }
+      if constexpr (kPaged) {
+        a_rh = n_rh;
+        if (uu + 2 < u_hi) tile_entries(p, n_rh, n_t, has, g, ahead);
+      } else {
+        if (uu + 1 < u_hi) tile_entries(p, n_rh, n_t, has, g, nxt);
+      }
       uint32_t nib = 0;
       bool bad = false;
 #pragma unroll

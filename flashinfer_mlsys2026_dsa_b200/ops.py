@@ -167,6 +167,72 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
         output.copy_(out_t)
 
 
+def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, page_table, positions, sm_scale, output,
+                 lse, page_size=None) -> None:
+    """:func:`kernel` with the slot ids formed in the kernel from a page table.
+
+    ``positions`` [B, topk] int32 are token positions in each row's sequence (-1 =
+    padding) and ``page_table`` [B, max_pages] int32 lists each row's pool pages; the
+    kernel gathers slot ``page_table[b, pos // page_size] * page_size + pos % page_size``,
+    the flat id the reference's callers build for ``sparse_indices`` (its pools are
+    flattened as page * 64 + offset, fused.py:155-156).  ``page_size`` defaults to the
+    pools' page dimension (``ckv_cache.shape[-2]`` of a [P, page_size, 512] pool).  A
+    position past the row's table or on a negative page is treated as padding and
+    flagged in :func:`read_device_errors`.
+    """
+    _validate(q_nope, q_pe, ckv_cache, kpe_cache, positions, output, lse)
+    if not isinstance(page_table, torch.Tensor) or not page_table.is_cuda:
+        raise ValueError("page_table must be a CUDA tensor")
+    if page_table.device != q_nope.device:
+        raise ValueError(f"page_table is on {page_table.device}, expected {q_nope.device}")
+    if page_table.dtype != torch.int32:
+        raise TypeError(f"page_table must be int32, got {page_table.dtype}")
+    B, H, _ = q_nope.shape
+    if page_table.dim() != 2 or page_table.shape[0] != B or page_table.shape[1] < 1:
+        raise ValueError(f"page_table must be [{B}, max_pages], got {tuple(page_table.shape)}")
+    if page_size is None:
+        if ckv_cache.dim() != 3:
+            raise ValueError("page_size is required for a pool that is not [pages, page_size, 512]")
+        page_size = ckv_cache.shape[-2]
+    page_size = int(page_size)
+    if page_size < 1 or page_size & (page_size - 1):
+        raise ValueError(f"page_size must be a power of two, got {page_size}")
+    if B == 0:
+        return
+    lib = _native._lib or _native.load()
+    topk = positions.shape[1]
+    if q_nope.stride(-1) != 1:
+        q_nope = q_nope.contiguous()
+    if q_pe.stride(-1) != 1:
+        q_pe = q_pe.contiguous()
+    if positions.stride(-1) != 1:
+        positions = positions.contiguous()
+    if page_table.stride(-1) != 1:
+        page_table = page_table.contiguous()
+    ckv = _slot_view(ckv_cache, D_CKV)
+    kpe = _slot_view(kpe_cache, D_KPE)
+    if ckv.shape[0] != kpe.shape[0]:
+        raise ValueError("ckv_cache and kpe_cache hold different slot counts")
+    out_t = output if output.stride(-1) == 1 else torch.empty_like(output, memory_format=torch.contiguous_format)
+    dev_index = q_nope.get_device()
+    stream = torch._C._cuda_getCurrentRawStream(dev_index)
+    ws = workspace_for(q_nope.device, stream, B, H, topk)
+    rc = lib.dsa_sparse_mla_decode_paged(
+        q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
+        q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
+        ckv.data_ptr(), ckv.stride(0),
+        kpe.data_ptr(), kpe.stride(0), ckv.shape[0],
+        page_table.data_ptr(), page_table.stride(0), page_table.shape[1], page_size,
+        positions.data_ptr(), positions.stride(0),
+        float(sm_scale),
+        out_t.data_ptr(), out_t.stride(0), out_t.stride(1),
+        lse.data_ptr(), lse.stride(0), lse.stride(1),
+        B, H, topk, ws.data_ptr(), ws.numel(), stream)
+    _check(rc, "dsa_sparse_mla_decode_paged")
+    if out_t is not output:
+        output.copy_(out_t)
+
+
 def decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):
     """Value-returning form of :func:`kernel`: returns (output, lse)."""
     B, H, _ = q_nope.shape

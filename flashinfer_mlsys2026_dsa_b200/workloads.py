@@ -48,6 +48,10 @@ class Workload:
     sparse_indices: torch.Tensor
     sm_scale: float
     seq_lens: list = field(default_factory=list)
+    # the inputs the slot ids were built from: each row's pool pages (-1 past the row's
+    # pages) and the selected token positions (-1 = padding)
+    page_table: torch.Tensor | None = None
+    positions: torch.Tensor | None = None
 
     @property
     def num_tokens(self) -> int:
@@ -161,4 +165,11 @@ def make(name: str, device="cuda", seed: int = 0, rank: int = 0, world_size: int
     q_pe = normal((B, H, D_KPE), 1.0)
     ckv = normal((P, PAGE, D_CKV), cfg["kv_scale"])
     kpe = normal((P, PAGE, D_KPE), cfg["kv_scale"])
-    return Workload(name, q_nope, q_pe, ckv, kpe, slots.contiguous(), 1.0 / math.sqrt(192.0), seq)
+    maxp = max(npages)
+    j = torch.arange(maxp, device=device)
+    np_t = torch.tensor(npages, dtype=torch.int64, device=device)
+    page_table = torch.where(j[None, :] < np_t[:, None],
+                             perm[(offs[:, None] + j[None, :]).clamp(max=P - 1)],
+                             torch.full((B, maxp), -1, dtype=perm.dtype, device=device))
+    return Workload(name, q_nope, q_pe, ckv, kpe, slots.contiguous(), 1.0 / math.sqrt(192.0), seq,
+                    page_table.to(torch.int32).contiguous(), pos.to(torch.int32).contiguous())

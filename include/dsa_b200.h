@@ -84,6 +84,35 @@ int dsa_sparse_mla_decode(const void* q_nope, int64_t q_nope_stride_b, int64_t q
                           int32_t topk, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The same decode with the index production step fused into the gather: the caller
+ * passes each row's token positions and page table instead of flat slot ids, and the
+ * kernel forms slot = page_table[row][pos / page_size] * page_size + pos % page_size
+ * as it fetches the slots, so the slot ids never travel through HBM.  Replaces the
+ * caller-side step that builds `sparse_indices` for the reference's entry point
+ * (fused.py:150; its pools are flattened as page * 64 + offset at fused.py:155-156 and
+ * baseline.py:17-23); the reference has no such entry point.
+ *
+ *   page_table [num_tokens, >= page_table_cols] int32, row stride page_table_stride_b:
+ *              row b lists the pool pages of row b's sequence in order
+ *   positions  [num_tokens, topk] int32, row stride positions_stride_b: token
+ *              positions within the row's sequence, -1 = padding
+ *   page_size  the pool's page size (a power of two; 64 for the reference's pools)
+ *
+ * A position < -1 or past the row's table (pos / page_size >= page_table_cols), or one
+ * whose page id is negative, is treated as padding and sets DSA_DEVERR_BAD_INDEX, like
+ * an out-of-range slot id.  Other arguments as for dsa_sparse_mla_decode().
+ */
+int dsa_sparse_mla_decode_paged(
+    const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h, const void* q_pe,
+    int64_t q_pe_stride_b, int64_t q_pe_stride_h, const void* ckv_cache, int64_t ckv_slot_stride,
+    const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots, const int32_t* page_table,
+    int64_t page_table_stride_b, int32_t page_table_cols, int32_t page_size,
+    const int32_t* positions, int64_t positions_stride_b, float sm_scale, void* output,
+    int64_t output_stride_b, int64_t output_stride_h, float* lse, int64_t lse_stride_b,
+    int64_t lse_stride_h, int64_t num_tokens, int32_t num_heads, int32_t topk, void* workspace,
+    size_t workspace_bytes, void* stream);
+
+/*
  * Bytes of workspace dsa_sparse_mla_decode() needs for this problem on
  * `device` (split-K partials and the error word; the size depends only on
  * the device's SM count, so one workspace serves every shape).

@@ -139,6 +139,28 @@ def decode_numpy(q_nope, q_pe, ckv, kpe, sparse_indices, sm_scale):
     return f32_to_bf16_bits(out), lse
 
 
+def slots_from_positions(page_table: np.ndarray, positions: np.ndarray, page_size: int):
+    """Index production: token positions + page table -> flat slot ids.
+
+    slot = page_table[b, pos // page_size] * page_size + pos % page_size, the flat slot
+    of a [pages, page_size, D] pool flattened to rows (baseline.py:17-23 and
+    fused.py:155-156 flatten the pools; the reference's callers pass such ids as
+    ``sparse_indices``).  -1 stays padding; a position < -1, past the row's table, or
+    on a negative page gives -2 (an invalid id: padding plus a bad-index flag in the
+    CUDA path).  Pure numpy, any size.
+    """
+    pt = np.asarray(page_table, dtype=np.int64)
+    pos = np.asarray(positions, dtype=np.int64)
+    cols = pt.shape[1]
+    page_idx = np.where(pos >= 0, pos // page_size, 0)
+    in_table = (pos >= 0) & (page_idx < cols)
+    page = np.take_along_axis(pt, np.where(in_table, page_idx, 0), axis=1)
+    slot = page * page_size + np.where(pos >= 0, pos % page_size, 0)
+    ok = in_table & (page >= 0) & (slot <= np.iinfo(np.int32).max)
+    out = np.where(ok, slot, np.where(pos == -1, -1, -2))
+    return out.astype(np.int32)
+
+
 def compact_pool(ckv_rows_fn, kpe_rows_fn, sparse_indices: np.ndarray):
     """Gather only the referenced slots so the oracle runs on a small pool.
 
