@@ -196,7 +196,29 @@ int device_sms(int dev) {
   return g_dev[dev].sms;
 }
 
-// Sets the decode kernel's shared-memory attribute and returns how many of its clusters
+using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, Params);
+struct KernelVariant {
+  int nh;       // heads per work unit
+  bool paged;   // slot ids formed from page tables
+  DecodeKernelFn fn;
+  int smem;
+};
+const KernelVariant kVariants[] = {
+    {16, false, h16::dsa_decode_h16_kernel<16, false>, h16::Cfg<16>::SMEM_BYTES},
+    {16, true, h16::dsa_decode_h16_kernel<16, true>, h16::Cfg<16>::SMEM_BYTES},
+    {32, false, h16::dsa_decode_h16_kernel<32, false>, h16::Cfg<32>::SMEM_BYTES},
+    {32, true, h16::dsa_decode_h16_kernel<32, true>, h16::Cfg<32>::SMEM_BYTES},
+};
+const KernelVariant& variant(int nh, bool paged) {
+  for (const KernelVariant& kv : kVariants)
+    if (kv.nh == nh && kv.paged == paged) return kv;
+  return kVariants[0];
+}
+// Heads per work unit: 16 for 16-head rows, 32 otherwise (a 128-head row is 4 units).
+int group_heads(int num_heads) { return num_heads == 16 ? 16 : 32; }
+constexpr size_t kMaxSlotFloats = (size_t)h16::Cfg<32>::kSlotFloats;
+
+// Sets the decode kernels' shared-memory attribute and returns how many of their clusters
 // fit on the device at once (the persistent grid's size), 0 on error.
 int device_pairs(int dev) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -205,21 +227,22 @@ int device_pairs(int dev) {
   if (d.pairs == 0) {
     // The kernel re-splits its register pool per warpgroup (setmaxnreg); refuse a build
     // whose pool is too small for that split, which would stall.
+    // every instance (16- or 32-head groups, flat or paged ids) must fit the same grid
     int n = 0;
-    for (auto kern : {h16::dsa_decode_h16_kernel<false>, h16::dsa_decode_h16_kernel<true>}) {
+    for (const KernelVariant& kv : kVariants) {
       cudaFuncAttributes fa;
-      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+      if (cudaFuncGetAttributes(&fa, kv.fn) != cudaSuccess) return 0;
       if ((int64_t)fa.numRegs * h16::kThreads < 256 * (int64_t)(h16::kRegsLow + h16::kRegsHigh))
         return 0;
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               h16::SMEM_BYTES) != cudaSuccess)
+      if (cudaFuncSetAttribute(kv.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kv.smem) !=
+          cudaSuccess)
         return 0;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (unsigned)(d.sms > 0 ? d.sms : 148), 1, 1);
       cfg.blockDim = dim3(h16::kThreads, 1, 1);
-      cfg.dynamicSmemBytes = h16::SMEM_BYTES;
+      cfg.dynamicSmemBytes = (size_t)kv.smem;
       int k = 0;
-      if (cudaOccupancyMaxActiveClusters(&k, kern, &cfg) != cudaSuccess || k <= 0) return 0;
+      if (cudaOccupancyMaxActiveClusters(&k, kv.fn, &cfg) != cudaSuccess || k <= 0) return 0;
       n = n == 0 ? k : (k < n ? k : n);
     }
     d.pairs = n;
@@ -235,10 +258,10 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Workspace layout, fixed for a device so that calls of any shape can share it:
 //   [0, 256)            header (word 0: sticky device error bits)
-//   [256, 8448)         split-K arrival counters of the 16-head kernel, 2 per CTA pair
-//                       (each returns to zero when its row is merged)
-//   [8448, ...)         split-K partials: 2 slots per decode CTA (or CTA pair), each
-//                       sized for the widest head group (64 heads)
+//   [256, 8448)         split-K arrival counters, 2 per CTA pair (one per rank; each
+//                       returns to zero when its row is merged)
+//   [8448, ...)         split-K partials: one slot per SM (at most one is used per CTA
+//                       pair), each sized for a 32-head group (O, m and l: 65,792 bytes)
 constexpr size_t kCountersOff = 256;
 constexpr size_t kPartsOff = 8448;
 constexpr int kMaxPairs = (int)((kPartsOff - kCountersOff) / 8);
@@ -251,7 +274,7 @@ WsLayout ws_layout(int sms) {
   WsLayout w;
   w.parts_off = kPartsOff;
   // one partial slot per cluster pair (at most one per two SMs; one per SM is room to spare)
-  w.total = align_up(w.parts_off + (size_t)sms * (size_t)h16::kSlotFloats * 4, 256);
+  w.total = align_up(w.parts_off + (size_t)sms * kMaxSlotFloats * 4, 256);
   return w;
 }
 
@@ -389,7 +412,8 @@ int check_args(const DecodeArgs& a) {
 
 // Which kernel a call runs, its persistent grid and the scratch it needs.
 struct Plan {
-  int tpr = 0;        // 96-slot tiles per (row, 16-head group)
+  int nh = 16;        // heads per work unit (16 or 32)
+  int tpr = 0;        // 96-slot tiles per (row, head group)
   int64_t units = 0;  // (row, group) pairs x tpr
   int grid = 0;       // cluster pairs of the persistent grid
   size_t need = 0;    // bytes of error header, counters and partials
@@ -398,7 +422,8 @@ struct Plan {
 int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
   const int cap = device_pairs(dev);
   if (cap <= 0) return DSA_ERR_CUDA;
-  const int hg = a.num_heads / h16::kNH;  // 16-head groups per row
+  pl.nh = group_heads(a.num_heads);
+  const int hg = a.num_heads / pl.nh;  // head groups per row
   pl.tpr = (a.topk + h16::kTS - 1) / h16::kTS;
   const int64_t num_rh = a.num_tokens * hg;
   pl.units = num_rh * (int64_t)pl.tpr;
@@ -410,7 +435,9 @@ int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
   const bool whole = num_rh <= cap;
   pl.grid = (int)(whole ? num_rh : cap);
   if (pl.grid > kMaxPairs) pl.grid = kMaxPairs;
-  pl.need = kPartsOff + (whole ? 0 : (size_t)pl.grid * (size_t)h16::kSlotFloats * 4);
+  const size_t slot_floats = pl.nh == 16 ? (size_t)h16::Cfg<16>::kSlotFloats
+                                         : (size_t)h16::Cfg<32>::kSlotFloats;
+  pl.need = kPartsOff + (whole ? 0 : (size_t)pl.grid * slot_floats * 4);
   return DSA_OK;
 }
 
@@ -436,14 +463,14 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   {
     cuuint64_t dims[3] = {(cuuint64_t)kDCkv, (cuuint64_t)a.num_heads, (cuuint64_t)a.num_tokens};
     cuuint64_t str[2] = {(cuuint64_t)a.qn_sh * 2, (cuuint64_t)a.qn_sb * 2};
-    cuuint32_t box[3] = {64, (cuuint32_t)h16::kNH, 1};
+    cuuint32_t box[3] = {64, (cuuint32_t)pl.nh, 1};
     if ((rc = encode(&m_qn, a.q_nope, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) != DSA_OK)
       return rc;
   }
   {
     cuuint64_t dims[3] = {(cuuint64_t)kDKpe, (cuuint64_t)a.num_heads, (cuuint64_t)a.num_tokens};
     cuuint64_t str[2] = {(cuuint64_t)a.qp_sh * 2, (cuuint64_t)a.qp_sb * 2};
-    cuuint32_t box[3] = {32, (cuuint32_t)h16::kNH, 1};
+    cuuint32_t box[3] = {32, (cuuint32_t)pl.nh, 1};
     if ((rc = encode(&m_qp, a.q_pe, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B)) != DSA_OK)
       return rc;
   }
@@ -458,7 +485,8 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   prm.lse_sh = a.lse_sh;
   prm.num_slots = a.num_slots;
   prm.units = pl.units;
-  prm.hg_shift = a.num_heads == 16 ? 0 : a.num_heads == 32 ? 1 : a.num_heads == 64 ? 2 : 3;
+  prm.hg_shift = 0;  // log2 of the head groups per row
+  while ((pl.nh << prm.hg_shift) < a.num_heads) ++prm.hg_shift;
   prm.topk = a.topk;
   prm.tpr = pl.tpr;
   prm.scale_log2 = a.sm_scale * kLog2e;
@@ -470,10 +498,9 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   prm.pt_cols = a.pt_cols;
   prm.pg_shift = 0;
   while (a.page_table != nullptr && (1 << prm.pg_shift) < a.page_size) ++prm.pg_shift;
-  auto kern = a.page_table != nullptr ? h16::dsa_decode_h16_kernel<true>
-                                      : h16::dsa_decode_h16_kernel<false>;
-  return launch_pdl(kern, dim3((unsigned)(2 * pl.grid)), dim3(h16::kThreads),
-                    (size_t)h16::SMEM_BYTES, st, m_ckv, m_kpe, m_qn, m_qp, prm);
+  const KernelVariant& kv = variant(pl.nh, a.page_table != nullptr);
+  return launch_pdl(kv.fn, dim3((unsigned)(2 * pl.grid)), dim3(h16::kThreads),
+                    (size_t)kv.smem, st, m_ckv, m_kpe, m_qn, m_qp, prm);
 }
 
 int current_device(int& dev) {

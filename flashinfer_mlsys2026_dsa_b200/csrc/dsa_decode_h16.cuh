@@ -1,10 +1,10 @@
-// DSA decode on two-CTA clusters, one 16-head group per work unit (H = 16, 32, 64 or 128:
-// a row with H heads is H/16 units that gather the same slots; the re-gathers of a row's
-// other groups mostly hit L2).
+// DSA decode on two-CTA clusters, one head group of one row per work unit: 16 heads for
+// H = 16, 32 heads for H = 32, 64, 128 (a row with H heads is H/NH units that gather the
+// same slots; the re-gathers of a row's other groups mostly hit L2).
 //
-// Why a pair: with 16 heads the score MMA is S^T[slots x 16] = K . Q^T, whose cost is
-// set by the number of MMA instructions (an M=128, N=16 MMA costs about as much as an
-// M=64 one), so a tile should be 128 rows of slots.  A whole 1152-byte slot per row,
+// Why a pair: with NH heads the score MMA is S^T[slots x NH] = K . Q^T, whose cost is
+// set by the number of MMA instructions (an M=128 MMA costs about as much as an M=64
+// one), so a tile should be 128 rows of slots.  A whole 1152-byte slot per row,
 // three stages deep (enough to hide the ~2-3 us gather latency under load), does not
 // fit in one SM's shared memory.  So each CTA of the pair owns half of every slot:
 //   rank r: ckv columns [256r, 256r + 256) (four 64-wide d-blocks, 128-byte swizzle)
@@ -13,23 +13,23 @@
 // over its 288 columns; the two partials are swapped through distributed shared
 // memory and both CTAs add them (own + peer: IEEE addition commutes, so both hold
 // bit-identical scores and take identical softmax decisions).  Each CTA then runs
-// PV over its own 256 value columns: O^T[256 d x 16] += V^T . P^T.
+// PV over its own 256 value columns: O^T[256 d x NH] += V^T . P^T.
 //
 // Per CTA (512 threads):
-//   warp 0        Q loader: the row's Q half (4 boxes of [16 x 64] + 1 of [16 x 32]).
+//   warp 0        Q loader: the unit's Q half (4 boxes of [NH x 64] + 1 of [NH x 32]).
 //   warps 1-5     gather producers, one per d-block (warp 5: the kpe half); lane g
 //                 issues one tile::gather4 (slots 4g..4g+3) per tile.
-//   warp 6        score MMA issuer: 18 MMAs (M=128, N=16) per tile.
-//   warp 7        PV MMA issuer: 12 MMAs (M=128, N=16) per tile.
+//   warp 6        score MMA issuer: 18 MMAs (M=128, N=NH) per tile.
+//   warp 7        PV MMA issuer: 12 MMAs (M=128, N=NH) per tile.
 //                 Two issuers, because an issuer's own shared-memory accesses (its
 //                 barrier waits) queue behind the tensor core's operand reads; with one
 //                 issuer those stalls, not the tensor core, set the tile period.
 //   warps 8-15    softmax / epilogue: warp w reads TMEM lanes 32(w%4).. (slots) and
-//                 handles heads 8((w-8)/4) .. +7.
-// The work split is stream-K over (row, 96-slot tile) units per pair, with the generic
-// kernel's split-K partial layout; a row cut between pairs is merged inside this kernel
-// by the pair holding its first tiles (per rank, for its value half), after a bounded
-// wait for the other pairs' partials.  Every wait is bounded.
+//                 handles heads (NH/2)((w-8)/4) .. + NH/2 - 1.
+// The work split is stream-K over (row, 96-slot tile) units per pair; a row cut between
+// pairs is merged inside this kernel by the pair holding its first tiles (per rank, for
+// its value half), after a bounded wait for the other pairs' partials.  Every wait is
+// bounded.
 #pragma once
 
 namespace dsa {
@@ -37,7 +37,6 @@ namespace h16 {
 
 constexpr int kTS = 96;                  // slots per tile; the score MMA is M=128 and its
                                          // rows >= kTS read past the region (never used)
-constexpr int kNH = 16;
 constexpr int kBlk = 4;                  // 64-wide ckv d-blocks per CTA
 constexpr int kRB = kTS * 128;           // one ckv d-block region of a stage
 constexpr int kRK = kTS * 64;            // the 32-wide kpe region of a stage
@@ -45,22 +44,7 @@ constexpr int kStageB = kBlk * kRB + kRK;
 constexpr int kStages = 3;
 constexpr int kGroups = kTS / 4;         // gather4 copies per d-block per tile
 constexpr int kPVKs = kTS / 16;          // K steps of one PV MMA chain
-constexpr int kQB = kBlk * 2048 + 1024;  // one Q buffer: 4 x [16 x 64] SW128 + [16 x 32] SW64
-constexpr int kPB = 4096;                // P^T [16 x 128 slots] bf16, SW128 K-major; one
-                                         // per stage: stage s is refilled only after the PV
-                                         // that read P[s] completed, so P[s] is then free
-constexpr int kXB = kTS * kNH * 4;       // partial scores from the peer, fp32 [kTS][16]
 constexpr int OFF_KV = 0;
-constexpr int OFF_Q = kStages * kStageB;
-constexpr int OFF_P = OFF_Q + 2 * kQB;
-constexpr int OFF_X = OFF_P + kStages * kPB;
-constexpr int OFF_BAR = OFF_X + 2 * kXB;
-constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
-constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain flag,
-                                         // [6] the peer's abort flag (written at exit)
-constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][8 heads] floats
-constexpr int SMEM_USED = OFF_RED + 2 * 4 * 8 * 4;
-constexpr int SMEM_BYTES = SMEM_USED + 1024;
 constexpr int kThreads = 512;
 constexpr int kQWarp = 0;
 constexpr int kProd0 = 1;
@@ -76,11 +60,50 @@ constexpr uint32_t kNamedBar = 1;
 constexpr uint32_t kRegsLow = 72;
 constexpr uint32_t kRegsHigh = 184;
 static_assert(256 * (kRegsLow + kRegsHigh) <= 65536, "register split exceeds the pool");
-constexpr int TMEM_COLS = 64;
-constexpr int S_COL = 0;   // two score buffers x 16 columns
-constexpr int O_COL = 32;  // two 128-d tiles x 16 columns
 constexpr uint32_t kSw128 = 2, kSw64 = 4;  // UMMA descriptor layout types
-constexpr int kSlotFloats = kNH * kDCkv + 2 * kNH;
+
+// What depends on the head-group width NH (the N of both MMAs): 16 for H = 16, 32 for
+// H = 32, 64, 128 (a 128-head row is then 4 units instead of 8, each tile doing twice the
+// head work for about the same fixed cost).  With 32 heads the Q half and the exchange
+// buffer double, so Q is single-buffered (a segment's Q loads once its predecessor's
+// last score is done) and P has two buffers (softmax waits for the PV two tiles back).
+template <int NH>
+struct Cfg {
+  static_assert(NH == 16 || NH == 32, "head group width");
+  static constexpr int kHT = NH / 2;               // heads per softmax thread
+  static constexpr int kQBufs = NH == 16 ? 2 : 1;
+  static constexpr int kPBufs = NH == 16 ? kStages : 2;
+  // exchange buffers: four let softmax send tile i+1's partial before finishing tile i
+  // (see the softmax loop); with 32 heads only two fit
+  static constexpr int kXBufs = NH == 16 ? 4 : 2;
+  static constexpr int kQBlk = NH * 128;           // one [NH x 64] SW128 Q block
+  static constexpr int kQB = kBlk * kQBlk + NH * 64;  // + the [NH x 32] SW64 q_pe block
+  static constexpr int kPBlk = NH * 128;           // P^T: [NH x 64 slots] bf16 SW128 block
+  static constexpr int kPB = 2 * kPBlk;            // P^T [NH x 128 slots], K-major
+  static constexpr int kXB = kTS * NH * 4;         // partial scores from the peer [kTS][NH]
+  static constexpr int OFF_Q = kStages * kStageB;
+  static constexpr int OFF_P = OFF_Q + kQBufs * kQB;
+  static constexpr int OFF_X = OFF_P + kPBufs * kPB;
+  static constexpr int OFF_BAR = OFF_X + kXBufs * kXB;
+  static constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
+  static constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain
+                                                  // flag, [6] the peer's abort flag (at exit)
+  static constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][kHT heads] floats
+  static constexpr int SMEM_USED = OFF_RED + 2 * 4 * kHT * 4;
+  static constexpr int SMEM_BYTES = SMEM_USED + 1024;
+  static constexpr int TMEM_COLS = NH == 16 ? 64 : 128;
+  static constexpr int S_COL = 0;        // two score buffers x NH columns
+  static constexpr int O_COL = 2 * NH;   // two 128-d tiles x NH columns
+  static constexpr int kSlotFloats = NH * kDCkv + 2 * NH;  // split-K partial: O, m, l
+
+  static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && kStageB % 1024 == 0 &&
+                    kQB % 1024 == 0 && kPB % 1024 == 0,
+                "128-byte swizzle atoms need 1024-byte alignment");
+  static_assert((kBlk * kRB) % 512 == 0 && (kBlk * kQBlk) % 512 == 0,
+                "64-byte swizzle atoms need 512-byte alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(kHT % 8 == 0, "softmax threads move heads in groups of 8 columns");
+};
 
 enum : int {
   B_KVF = 0,                     // [stage] landed: one arrive (with its bytes) per producer
@@ -91,21 +114,21 @@ enum : int {
   B_QF = B_KVE + kStages * 5, B_QE = B_QF + 2,
   B_SF = B_QE + 2, B_SE = B_SF + 2,  // score buffer full / read
   B_PF = B_SE + 2, B_PD = B_PF + 2,  // P written (+ O rescaled) / PV done
-  B_XF = B_PD + 2,               // [2] the peer's partial scores are in X[b] (complete_tx)
-  B_OF = B_XF + 2,               // the epilogue has read O
+  B_XF = B_PD + 2,               // [kXBufs <= 4] the peer's partial scores are in X[b]
+                                 // (complete_tx)
+  B_OF = B_XF + 4,               // the epilogue has read O
   B_DRAIN = B_OF + 1,            // [2] used only when an issuer stops early
   B_COUNT = B_DRAIN + 2
 };
 __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * 5 + blk; }
-// X[b] needs no "empty" barrier: the peer writes X[b] for tile i + 2 only after it has
-// received this CTA's partial of tile i + 1, which this CTA sends after it has read
-// X[b] for tile i (tiles are processed in order on both sides).
+// The exchange buffers X need no "empty" barrier.  A thread sends its partial of tile j
+// (into the peer's X[j % kXBufs]) only after it finished tile j - 2, whose X wait needed
+// every peer thread's partial of tile j - 2; a peer thread sends that only after it
+// finished tile j - 4 (in the look-ahead order) or j - 3 (in plain order).  So X[b] is
+// rewritten only after both sides have read it: four buffers suffice for the look-ahead
+// order, two for the plain order (a thread then sends tile j after finishing tile j - 1,
+// and the same argument gives j - 2).
 
-static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && kStageB % 1024 == 0 && kQB % 1024 == 0,
-              "128-byte swizzle atoms need 1024-byte alignment");
-static_assert((kBlk * kRB) % 512 == 0 && (kBlk * 2048) % 512 == 0,
-              "64-byte swizzle atoms need 512-byte alignment");
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 static_assert(B_COUNT * 8 <= 512, "barrier block");
 static_assert(kTS % 16 == 0 && kTS <= 128 && kGroups <= 32, "tile shape");
 static_assert(kStages * 4 * 4 <= 64, "mask words");
@@ -159,13 +182,20 @@ __device__ __forceinline__ void translate(const Params& p, int64_t rh, const int
 // kPaged: sparse_indices holds token positions, translated through the page table by the
 // gather producers (ids are fetched two tiles ahead so the dependent page-table load is off
 // the producer's path).
-template <bool kPaged>
+template <int NH, bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dsa_decode_h16_kernel(const __grid_constant__ CUtensorMap tm_ckv,
                           const __grid_constant__ CUtensorMap tm_kpe,
                           const __grid_constant__ CUtensorMap tm_qn,
                           const __grid_constant__ CUtensorMap tm_qp,
                           const __grid_constant__ Params p) {
+  using C = Cfg<NH>;
+  constexpr int kHT = C::kHT, kQBufs = C::kQBufs, kPBufs = C::kPBufs, kXBufs = C::kXBufs;
+  constexpr int kQB = C::kQB, kPB = C::kPB, kXB = C::kXB;
+  constexpr int OFF_Q = C::OFF_Q, OFF_P = C::OFF_P, OFF_X = C::OFF_X, OFF_BAR = C::OFF_BAR;
+  constexpr int OFF_MASK = C::OFF_MASK, OFF_MISC = C::OFF_MISC, OFF_RED = C::OFF_RED;
+  constexpr int TMEM_COLS = C::TMEM_COLS, S_COL = C::S_COL, O_COL = C::O_COL;
+  constexpr int kSlotFloats = C::kSlotFloats;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
@@ -192,10 +222,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::mbar_init(bar(B_SE + b), kSmWarps);  // one arrive per softmax warp
       ptx::mbar_init(bar(B_PF + b), kSmWarps);
       ptx::mbar_init(bar(B_PD + b), 1);
-      // X[b] is full once this CTA armed it (one arrive with the expected bytes) and the
-      // peer's st.async bytes landed; the peer's stores may come before the arming.
-      ptx::mbar_init(bar(B_XF + b), 1);
     }
+    // X[b] is full once this CTA armed it (one arrive with the expected bytes) and the
+    // peer's st.async bytes landed; the peer's stores may come before the arming.
+    for (int b = 0; b < kXBufs; ++b) ptx::mbar_init(bar(B_XF + b), 1);
     ptx::mbar_init(bar(B_OF), kSmWarps);
     ptx::mbar_init(bar(B_DRAIN), 1);
     ptx::mbar_init(bar(B_DRAIN + 1), 1);
@@ -203,8 +233,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     misc[3] = 0;
     misc[6] = 0;
     ptx::fence_mbar_init();
-    ptx::mbar_arrive_expect_tx(bar(B_XF + 0), (uint32_t)kXB);
-    ptx::mbar_arrive_expect_tx(bar(B_XF + 1), (uint32_t)kXB);
+    for (int b = 0; b < kXBufs; ++b) ptx::mbar_arrive_expect_tx(bar(B_XF + b), (uint32_t)kXB);
   }
   if (warp == kQWarp && lane == 0) {
     ptx::prefetch_tmap(&tm_ckv);
@@ -240,22 +269,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int64_t u = u_lo;
       Segment s;
       while (next_segment(u, u_hi, p.tpr, s)) {
-        const int qb = seg & 1;
-        if (!wait(bar(B_QE + qb), (uint32_t)(((seg >> 1) & 1) ^ 1))) break;
+        const int qb = seg % kQBufs;
+        if (!wait(bar(B_QE + qb), (uint32_t)(((seg / kQBufs) & 1) ^ 1))) break;
         ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)kQB);
         const uint32_t qd = sbase + (uint32_t)(OFF_Q + qb * kQB);
         const int b = (int)(s.rh >> p.hg_shift);
-        const int h0 = kNH * (int)(s.rh & ((1 << p.hg_shift) - 1));
+        const int h0 = NH * (int)(s.rh & ((1 << p.hg_shift) - 1));
         for (int j = 0; j < kBlk; ++j)
-          ptx::tma_load_3d(qd + (uint32_t)(j * 2048), &tm_qn, (int)(256 * rank) + 64 * j, h0, b,
-                           bar(B_QF + qb));
-        ptx::tma_load_3d(qd + (uint32_t)(kBlk * 2048), &tm_qp, (int)(32 * rank), h0, b,
+          ptx::tma_load_3d(qd + (uint32_t)(j * C::kQBlk), &tm_qn, (int)(256 * rank) + 64 * j, h0,
+                           b, bar(B_QF + qb));
+        ptx::tma_load_3d(qd + (uint32_t)(kBlk * C::kQBlk), &tm_qp, (int)(32 * rank), h0, b,
                          bar(B_QF + qb));
         ++seg;
       }
       if (seg > 0) {
         const Waiter drain{misc + 3, p.err};
-        drain(bar(B_QF + ((seg - 1) & 1)), (uint32_t)(((seg - 1) >> 1) & 1));
+        drain(bar(B_QF + ((seg - 1) % kQBufs)), (uint32_t)(((seg - 1) / kQBufs) & 1));
       }
     }
     __syncwarp();
@@ -367,24 +396,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::regs_dec<kRegsLow>();
     if (lane == 0) {
       const Waiter wait{misc + 2, p.err, true};
-      constexpr uint32_t kIdS = idesc_bf16(128, kNH, false);
+      constexpr uint32_t kIdS = idesc_bf16(128, NH, false);
       // Descriptors of offset 0; an operand at byte offset o adds o >> 4.
       const uint64_t dk = desc(sbase + (uint32_t)OFF_KV, 16, 1024, kSw128);
       const uint64_t dkp = desc(sbase + (uint32_t)(OFF_KV + kBlk * kRB), 16, 512, kSw64);
       const uint64_t dq = desc(sbase + (uint32_t)OFF_Q, 16, 1024, kSw128);
-      const uint64_t dqp = desc(sbase + (uint32_t)(OFF_Q + kBlk * 2048), 16, 512, kSw64);
+      const uint64_t dqp = desc(sbase + (uint32_t)(OFF_Q + kBlk * C::kQBlk), 16, 512, kSw64);
       int64_t i = 0;
       int seg = 0;
       bool ok = true;
       int64_t u = u_lo;
       Segment s;
       while (ok && next_segment(u, u_hi, p.tpr, s)) {
-        const int qb = seg & 1;
+        const int qb = seg % kQBufs;
         const uint64_t qo = (uint64_t)((qb * kQB) >> 4);
         for (int t = s.t0; t < s.t1; ++t, ++i) {
           const int st = (int)(i % kStages);
           const int sb = (int)(i & 1);
-          if (t == s.t0) ok = wait(bar(B_QF + qb), (uint32_t)((seg >> 1) & 1));
+          if (t == s.t0) ok = wait(bar(B_QF + qb), (uint32_t)((seg / kQBufs) & 1));
           ok = ok && wait(bar(B_SE + sb), (uint32_t)(((i >> 1) & 1) ^ 1));
           ok = ok && wait(bar(B_KVF + st), (uint32_t)((i / kStages) & 1));
           if (!ok) break;
@@ -392,14 +421,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           // skips its MMAs (its scores are all masked).
           if (masks[st * 4 + 3] != 0u) {
             ptx::tc_fence_after();
-            const uint32_t d_s = tmem + (uint32_t)(S_COL + 16 * sb);
+            const uint32_t d_s = tmem + (uint32_t)(S_COL + NH * sb);
             const uint64_t ko = (uint64_t)((st * kStageB) >> 4);
 #pragma unroll
             for (int j = 0; j < kBlk; ++j)
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
                 ptx::umma_bf16(d_s, dk + ko + (uint64_t)((j * kRB + ks * 32) >> 4),
-                               dq + qo + (uint64_t)((j * 2048 + ks * 32) >> 4), kIdS,
+                               dq + qo + (uint64_t)((j * C::kQBlk + ks * 32) >> 4), kIdS,
                                (j | ks) ? 1u : 0u);
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
@@ -427,7 +456,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::regs_dec<kRegsLow>();
     if (lane == 0) {
       const Waiter wait{misc + 2, p.err, true};
-      constexpr uint32_t kIdPV = idesc_bf16(128, kNH, true);
+      constexpr uint32_t kIdPV = idesc_bf16(128, NH, true);
       const uint64_t dv = desc(sbase + (uint32_t)OFF_KV, kRB, 1024, kSw128);
       const uint64_t dp = desc(sbase + (uint32_t)OFF_P, 16, 1024, kSw128);
       int64_t j = 0;
@@ -448,14 +477,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (masks[st * 4 + 3] != 0u) {
             ptx::tc_fence_after();
             const uint64_t vo = (uint64_t)((st * kStageB) >> 4);
-            const uint64_t po = (uint64_t)((st * kPB) >> 4);
+            const uint64_t po = (uint64_t)(((int)(j % kPBufs) * kPB) >> 4);
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
               for (int ks = 0; ks < kPVKs; ++ks)
-                ptx::umma_bf16(tmem + (uint32_t)(O_COL + 16 * mt),
+                ptx::umma_bf16(tmem + (uint32_t)(O_COL + NH * mt),
                                dv + vo + (uint64_t)((2 * mt * kRB + ks * 2048) >> 4),
-                               dp + po + (uint64_t)(((ks >> 2) * 2048 + (ks & 3) * 32) >> 4),
+                               dp + po + (uint64_t)(((ks >> 2) * C::kPBlk + (ks & 3) * 32) >> 4),
                                kIdPV, (o_init || ks > 0) ? 1u : 0u);
               // value d-blocks 2mt, 2mt+1 are free once this half's MMAs are done
               ptx::umma_commit(bar(kve(st, 2 * mt)));
@@ -480,7 +509,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ softmax / epilogue
     ptx::regs_inc<kRegsHigh>();
     const int qd = warp & 3;               // TMEM lane quadrant = slots 32qd .. 32qd+31
-    const int hh = (warp - kSm0) >> 2;     // heads 8hh .. 8hh+7
+    const int hh = (warp - kSm0) >> 2;     // heads kHT*hh .. kHT*hh + kHT-1
     const int slot = 32 * qd + lane;
     const bool slot_ok = slot < kTS;
     const uint32_t lane_base = (uint32_t)(32 * qd) << 16;
@@ -492,134 +521,191 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool aborted = false;
     int64_t u = u_lo;
     Segment s;
-    float m_run[8], l_part[8];
+    float m_run[kHT], l_part[kHT];
     while (!aborted && next_segment(u, u_hi, p.tpr, s)) {
 #pragma unroll
-      for (int h = 0; h < 8; ++h) {
+      for (int h = 0; h < kHT; ++h) {
         m_run[h] = -INFINITY;
         l_part[h] = 0.f;
       }
       bool o_valid = false;
-      for (int t = s.t0; t < s.t1; ++t, ++i) {
-        const int st = (int)(i % kStages);
-        const int sb = (int)(i & 1);
-        bool ok = !aborted && wait(bar(B_KVF + st), (uint32_t)((i / kStages) & 1)) &&
-                  wait(bar(B_SF + sb), (uint32_t)((i >> 1) & 1));
-        const uint32_t mw = qd < 3 ? masks[st * 4 + qd] : 0u;
-        const bool live = masks[st * 4 + 3] != 0u;
-        const bool valid = slot_ok && ((mw >> lane) & 1u);
+      // Two halves per tile: A(i) reads tile i's partial scores from TMEM and sends them to
+      // the peer; B(i) waits for the peer's partial, runs the online softmax and writes P.
+      // With four exchange buffers a warp whose next score is already done runs A(i+1)
+      // before B(i), so the exchange latency of tile i+1 overlaps the softmax of tile i;
+      // otherwise (or with two buffers) it runs B(i) first, as a plain sequence would.
+      uint32_t own_prev[kHT];  // the in-flight tile's own partial scores
+      auto fetch_send = [&](int64_t ic, uint32_t* own) -> bool {
+        const int st = (int)(ic % kStages);
+        const int sb = (int)(ic & 1);
+        const int xb = (int)(ic % kXBufs);
+        const bool ok = !aborted && wait(bar(B_KVF + st), (uint32_t)((ic / kStages) & 1)) &&
+                        wait(bar(B_SF + sb), (uint32_t)((ic >> 1) & 1));
         ptx::tc_fence_after();
-        uint32_t own[8];
-        ptx::tmem_ld8(tmem + lane_base + (uint32_t)(S_COL + 16 * sb + 8 * hh), own);
+#pragma unroll
+        for (int c = 0; c < kHT; c += 8)
+          ptx::tmem_ld8(tmem + lane_base + (uint32_t)(S_COL + NH * sb + kHT * hh + c), own + c);
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
         // One arrive per warp (a barrier arrive is an atomic on one shared word: 256 of them
         // would serialise); the warp's lanes agree first.
         if (__all_sync(0xffffffffu, ok) && lane == 0) ptx::mbar_arrive(bar(B_SE + sb));
-        // Swap partial scores with the peer: st.async ours into its X[sb] (completing its
-        // B_XF[sb] by bytes), then wait for its bytes in ours.
+        // st.async our partial into the peer's X[xb], completing its B_XF[xb] by bytes.
         if (ok && slot_ok) {
-          const uint32_t a = x_peer + (uint32_t)(sb * kXB + slot * 64 + hh * 32);
-          const uint32_t xb = xf_peer + 8u * (uint32_t)sb;
-          ptx::st_async_v4(a, own[0], own[1], own[2], own[3], xb);
-          ptx::st_async_v4(a + 16u, own[4], own[5], own[6], own[7], xb);
+          const uint32_t a = x_peer + (uint32_t)(xb * kXB + slot * (NH * 4) + hh * (kHT * 4));
+          const uint32_t xfb = xf_peer + 8u * (uint32_t)xb;
+#pragma unroll
+          for (int c = 0; c < kHT; c += 4)
+            ptx::st_async_v4(a + 4u * (uint32_t)c, own[c], own[c + 1], own[c + 2], own[c + 3],
+                             xfb);
         }
-        ok = ok && wait(bar(B_XF + sb), (uint32_t)((i >> 1) & 1));
-        float x[8];
-        bool need = false;
+        return ok;
+      };
+      // a segment is never empty: A of its first tile, then per tile B(ip) and A(ip + 1)
+      bool ok_prev = fetch_send(i, own_prev);
+      int64_t ip = i++;  // the tile in flight
+      for (int t = s.t0 + 1;; ++t) {
+        const bool more = t < s.t1;
+        uint32_t own_cur[kHT];
+        bool ok_cur = false;
+        bool a_first = false;  // A(i) before B(ip): only when the next score is done
+        if constexpr (kXBufs >= 4) {
+          if (more)
+            a_first = __all_sync(0xffffffffu,
+                                 aborted || ptx::mbar_test_wait(bar(B_SF + (int)(i & 1)),
+                                                                (uint32_t)((i >> 1) & 1)));
+          if (a_first) ok_cur = fetch_send(i, own_cur);
+        }
         {
-          float4 pa = make_float4(0.f, 0.f, 0.f, 0.f), pb4 = pa;
-          if (slot_ok) {
-            const float* xs = reinterpret_cast<const float*>(sgen + OFF_X + sb * kXB + slot * 64 + hh * 32);
-            pa = *reinterpret_cast<const float4*>(xs);
-            pb4 = *reinterpret_cast<const float4*>(xs + 4);
-          }
-          // X[sb] is read: re-arm it for tile i + 2.
-          if (warp == kSm0 && lane == 0) ptx::mbar_arrive_expect_tx(bar(B_XF + sb), (uint32_t)kXB);
-          const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb4.x, pb4.y, pb4.z, pb4.w};
+          // ------------------------------------------------ B(ip): finish the tile in flight
+          const int st = (int)(ip % kStages);
+          const int xb = (int)(ip % kXBufs);
+          const uint32_t mw = qd < 3 ? masks[st * 4 + qd] : 0u;
+          const bool live = masks[st * 4 + 3] != 0u;
+          const bool valid = slot_ok && ((mw >> lane) & 1u);
+            bool ok = ok_prev && wait(bar(B_XF + xb), (uint32_t)((ip / kXBufs) & 1));
+            float x[kHT];
+            bool need = false;
+            {
+              float pr[kHT];
 #pragma unroll
-          for (int h = 0; h < 8; ++h) {
-            x[h] = valid ? (__uint_as_float(own[h]) + pr[h]) * p.scale_log2 : -INFINITY;
-            need |= x[h] > m_run[h] + kTau;
-          }
-        }
-        bool rescale = false;
-        if (ptx::bar_red_or(kNamedBar, kSmThreads, need || aborted || !ok)) {
-          if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !ok)) {
-            aborted = true;
-            break;
-          }
-          rescale = true;
-        }
-        if (rescale) {
-#pragma unroll
-          for (int h = 0; h < 8; ++h) {
-            float v = x[h];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-            if (lane == 0) red_max[(hh * 4 + qd) * 8 + h] = v;
-          }
-          ptx::bar_sync(kNamedBar, kSmThreads);
-          float alpha[8];
-#pragma unroll
-          for (int h = 0; h < 8; ++h) {
-            const float* r4 = red_max + hh * 32 + h;
-            const float mt = fmaxf(fmaxf(r4[0], r4[8]), fmaxf(r4[16], r4[24]));
-            const float mn = fmaxf(m_run[h], mt);
-            alpha[h] = (m_run[h] == -INFINITY) ? 0.f : ptx::ex2(m_run[h] - mn);
-            l_part[h] *= alpha[h];
-            m_run[h] = mn;
-          }
-          if (o_valid) {
-            // the outcome is made warp-uniform: the TMEM loads and stores below are
-            // warp-collective, and a warp continues or stops as one
-            const bool wok = wait(bar(B_PD + (int)((i - 1) & 1)), (uint32_t)(((i - 1) >> 1) & 1));
-            if (!__all_sync(0xffffffffu, wok)) {
-              aborted = true;
-            } else {
-              ptx::tc_fence_after();
-#pragma unroll
-              for (int mt = 0; mt < 2; ++mt) {
-                const uint32_t ta = tmem + lane_base + (uint32_t)(O_COL + 16 * mt + 8 * hh);
-                uint32_t rr[8];
-                ptx::tmem_ld8(ta, rr);
-                ptx::tmem_wait_ld();
-#pragma unroll
-                for (int h = 0; h < 8; ++h)
-                  rr[h] = __float_as_uint(__uint_as_float(rr[h]) * alpha[h]);
-                ptx::tmem_st8(ta, rr);
+              for (int c = 0; c < kHT; c += 4) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (slot_ok)
+                  v = *reinterpret_cast<const float4*>(
+                      sgen + OFF_X + xb * kXB + slot * (NH * 4) + hh * (kHT * 4) + 4 * c);
+                pr[c] = v.x;
+                pr[c + 1] = v.y;
+                pr[c + 2] = v.z;
+                pr[c + 3] = v.w;
               }
-              ptx::tmem_wait_st();
+              // X[xb] is read: re-arm it for tile ip + kXBufs.
+              if (warp == kSm0 && lane == 0) ptx::mbar_arrive_expect_tx(bar(B_XF + xb), (uint32_t)kXB);
+#pragma unroll
+              for (int h = 0; h < kHT; ++h) {
+                x[h] = valid ? (__uint_as_float(own_prev[h]) + pr[h]) * p.scale_log2 : -INFINITY;
+                need |= x[h] > m_run[h] + kTau;
+              }
             }
-          }
-        }
-        if (aborted) continue;  // the next vote ends the loop for every thread
-        uint8_t* pbuf = sgen + OFF_P + st * kPB + (slot >> 6) * 2048;
+            bool rescale = false;
+            if (ptx::bar_red_or(kNamedBar, kSmThreads, need || aborted || !ok)) {
+              if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !ok)) {
+                aborted = true;
+                break;
+              }
+              rescale = true;
+            }
+            if (rescale) {
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
-          const float pv = ptx::ex2(x[h] - me);
-          l_part[h] += pv;
-          if (live && slot_ok)
-            *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(8 * hh + h, slot & 63)) =
-                __float2bfloat16_rn(pv);
-        }
-        if (live && slot_ok && !valid) {
-          // A padded slot of a live tile: P is 0, but 0 * (stale non-finite bytes) would
-          // poison the PV sum, so clear this slot's value row (d-blocks 2hh, 2hh+1).
-          uint8_t* row = sgen + OFF_KV + st * kStageB + slot * 128;
+              for (int h = 0; h < kHT; ++h) {
+                float v = x[h];
 #pragma unroll
-          for (int jb = 0; jb < 2; ++jb)
+                for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+                if (lane == 0) red_max[(hh * 4 + qd) * kHT + h] = v;
+              }
+              ptx::bar_sync(kNamedBar, kSmThreads);
+              float alpha[kHT];
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-              *reinterpret_cast<uint4*>(row + (2 * hh + jb) * kRB + c * 16) =
-                  make_uint4(0u, 0u, 0u, 0u);
+              for (int h = 0; h < kHT; ++h) {
+                const float* r4 = red_max + hh * 4 * kHT + h;
+                const float mt = fmaxf(fmaxf(r4[0], r4[kHT]), fmaxf(r4[2 * kHT], r4[3 * kHT]));
+                const float mn = fmaxf(m_run[h], mt);
+                alpha[h] = (m_run[h] == -INFINITY) ? 0.f : ptx::ex2(m_run[h] - mn);
+                l_part[h] *= alpha[h];
+                m_run[h] = mn;
+              }
+              if (o_valid) {
+                // the outcome is made warp-uniform: the TMEM loads and stores below are
+                // warp-collective, and a warp continues or stops as one
+                const bool wok = wait(bar(B_PD + (int)((ip - 1) & 1)), (uint32_t)(((ip - 1) >> 1) & 1));
+                if (!__all_sync(0xffffffffu, wok)) {
+                  aborted = true;
+                } else {
+                  ptx::tc_fence_after();
+#pragma unroll
+                  for (int mt = 0; mt < 2; ++mt) {
+                    const uint32_t ta = tmem + lane_base + (uint32_t)(O_COL + NH * mt + kHT * hh);
+                    uint32_t rr[kHT];
+#pragma unroll
+                    for (int c = 0; c < kHT; c += 8) ptx::tmem_ld8(ta + (uint32_t)c, rr + c);
+                    ptx::tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < kHT; ++h)
+                      rr[h] = __float_as_uint(__uint_as_float(rr[h]) * alpha[h]);
+#pragma unroll
+                    for (int c = 0; c < kHT; c += 8) ptx::tmem_st8(ta + (uint32_t)c, rr + c);
+                  }
+                  ptx::tmem_wait_st();
+                }
+              }
+            }
+            if constexpr (kPBufs < kStages) {
+              // Fewer P buffers than stages: P[i % kPBufs] was last read by the PV of tile
+              // i - kPBufs, which must be done before it is overwritten (warp-uniform outcome).
+              if (live && ip >= kPBufs && !aborted) {
+                const int64_t iq = ip - kPBufs;
+                const bool wok = wait(bar(B_PD + (int)(iq & 1)), (uint32_t)((iq >> 1) & 1));
+                if (!__all_sync(0xffffffffu, wok)) aborted = true;
+              }
+            }
+            if (!aborted) {  // else the next vote ends the loop for every thread
+              uint8_t* pbuf = sgen + OFF_P + (int)(ip % kPBufs) * kPB + (slot >> 6) * C::kPBlk;
+#pragma unroll
+              for (int h = 0; h < kHT; ++h) {
+                const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
+                const float pv = ptx::ex2(x[h] - me);
+                l_part[h] += pv;
+                if (live && slot_ok)
+                  *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(kHT * hh + h, slot & 63)) =
+                      __float2bfloat16_rn(pv);
+              }
+              if (live && slot_ok && !valid) {
+                // A padded slot of a live tile: P is 0, but 0 * (stale non-finite bytes) would
+                // poison the PV sum, so clear this slot's value row (d-blocks 2hh, 2hh+1).
+                uint8_t* row = sgen + OFF_KV + st * kStageB + slot * 128;
+#pragma unroll
+                for (int jb = 0; jb < 2; ++jb)
+#pragma unroll
+                  for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(row + (2 * hh + jb) * kRB + c * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+              }
+              ptx::fence_proxy_async_smem();
+              ptx::tc_fence_before();
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(bar(B_PF + (int)(ip & 1)));
+              o_valid = o_valid || live;
+            }
         }
-        ptx::fence_proxy_async_smem();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar(B_PF + (int)(i & 1)));
-        o_valid = o_valid || live;
+        if (!more) break;
+        if (a_first) {
+#pragma unroll
+          for (int h = 0; h < kHT; ++h) own_prev[h] = own_cur[h];
+          ok_prev = ok_cur;
+        } else {
+          ok_prev = fetch_send(i, own_prev);  // own_prev is dead after B(ip)
+        }
+        ip = i++;
       }
       // ---------------------------------------------------------------- epilogue
       // Every thread votes here, also one that gave up after the last tile's vote.
@@ -632,22 +718,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       float* red_sum = red;  // the max slots are free again: every thread passed the vote
 #pragma unroll
-      for (int h = 0; h < 8; ++h) {
+      for (int h = 0; h < kHT; ++h) {
         float v = l_part[h];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) red_sum[(hh * 4 + qd) * 8 + h] = v;
+        if (lane == 0) red_sum[(hh * 4 + qd) * kHT + h] = v;
       }
       ptx::bar_sync(kNamedBar, kSmThreads);
-      float L[8];
+      float L[kHT];
 #pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        const float* r4 = red_sum + hh * 32 + h;
-        L[h] = (r4[0] + r4[8]) + (r4[16] + r4[24]);
+      for (int h = 0; h < kHT; ++h) {
+        const float* r4 = red_sum + hh * 4 * kHT + h;
+        L[h] = (r4[0] + r4[kHT]) + (r4[2 * kHT] + r4[3 * kHT]);
       }
-      const int64_t rh = s.rh;                        // (row, 16-head group)
+      const int64_t rh = s.rh;                        // (row, NH-head group)
       const int64_t b = rh >> p.hg_shift;
-      const int h0 = kNH * (int)(rh & ((1 << p.hg_shift) - 1));   // first head of the group
+      const int h0 = NH * (int)(rh & ((1 << p.hg_shift) - 1));   // first head of the group
       const bool full = (s.t0 == 0 && s.t1 == p.tpr);
       // A row cut between pairs: the pair holding its first tiles (the head, p_lo) ends
       // its range with them; the others start theirs with the rest and so finish early.
@@ -658,18 +744,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool head = full || pair == p_lo;
       // a pair writes a partial only for the row its range starts inside: one slot each
       float* part = p.parts + pair * kSlotFloats;
-      float o_mine[2][8];
+      float o_mine[2][kHT];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        uint32_t rr[8];
-        ptx::tmem_ld8(tmem + lane_base + (uint32_t)(O_COL + 16 * mt + 8 * hh), rr);
+        uint32_t rr[kHT];
+#pragma unroll
+        for (int c = 0; c < kHT; c += 8)
+          ptx::tmem_ld8(tmem + lane_base + (uint32_t)(O_COL + NH * mt + kHT * hh + c), rr + c);
         ptx::tmem_wait_ld();
         const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
+        for (int h = 0; h < kHT; ++h) {
           const float o = __uint_as_float(rr[h]);
           o_mine[mt][h] = o;
-          const int head_idx = 8 * hh + h;
+          const int head_idx = kHT * hh + h;
           if (full)
             p.out[b * p.out_sb + (int64_t)(h0 + head_idx) * p.out_sh + d] =
                 __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
@@ -677,23 +765,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             part[head_idx * kDCkv + d] = o;
         }
       }
-      if (qd == 0 && lane < 8) {
+      if (qd == 0 && lane < kHT) {
         float mh = 0.f, lh = 0.f;  // unrolled select keeps m_run / L in registers
 #pragma unroll
-        for (int h = 0; h < 8; ++h)
+        for (int h = 0; h < kHT; ++h)
           if (h == lane) {
             mh = m_run[h];
             lh = L[h];
           }
-        const int head_idx = 8 * hh + lane;
+        const int head_idx = kHT * hh + lane;
         if (full) {
           if (rank == 0)
             p.lse[b * p.lse_sb + (int64_t)(h0 + head_idx) * p.lse_sh] =
                 lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         } else if (!head) {
           // both ranks write the (identical) scalars, so each rank's merge finds them
-          part[kNH * kDCkv + head_idx] = mh;
-          part[kNH * kDCkv + kNH + head_idx] = lh;
+          part[NH * kDCkv + head_idx] = mh;
+          part[NH * kDCkv + NH + head_idx] = lh;
         }
       }
       uint32_t* cnt = p.counters + 2 * p_lo + rank;
@@ -719,9 +807,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         ptx::bar_sync(kNamedBar, kSmThreads);
-        float M[8], Lt[8], acc[2][8];
+        float M[kHT], Lt[kHT], acc[2][kHT];
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
+        for (int h = 0; h < kHT; ++h) {
           M[h] = m_run[h];
           Lt[h] = L[h];
           acc[0][h] = o_mine[0][h];
@@ -730,19 +818,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
           // a later pair's range starts inside this row: its partial is in its slot
           const float* pp = p.parts + cc * kSlotFloats;
-          float pm[8], pl[8], po[2][8];
+          float pm[kHT], pl[kHT], po[2][kHT];
           // every load of the part first, so that the part costs one L2 round trip
 #pragma unroll
-          for (int h = 0; h < 8; ++h) {
-            const int head_idx = 8 * hh + h;
-            pm[h] = __ldcg(pp + kNH * kDCkv + head_idx);
-            pl[h] = __ldcg(pp + kNH * kDCkv + kNH + head_idx);
+          for (int h = 0; h < kHT; ++h) {
+            const int head_idx = kHT * hh + h;
+            pm[h] = __ldcg(pp + NH * kDCkv + head_idx);
+            pl[h] = __ldcg(pp + NH * kDCkv + NH + head_idx);
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
               po[mt][h] = __ldcg(pp + head_idx * kDCkv + (int)(256 * rank) + 128 * mt + 32 * qd + lane);
           }
 #pragma unroll
-          for (int h = 0; h < 8; ++h) {
+          for (int h = 0; h < kHT; ++h) {
             // A part with l == 0 saw only padding; its O (maybe stale) is not used.
             const bool live = pl[h] > 0.f;
             const bool have = Lt[h] > 0.f;
@@ -760,19 +848,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int mt = 0; mt < 2; ++mt) {
           const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
 #pragma unroll
-          for (int h = 0; h < 8; ++h)
-            p.out[b * p.out_sb + (int64_t)(h0 + 8 * hh + h) * p.out_sh + d] =
+          for (int h = 0; h < kHT; ++h)
+            p.out[b * p.out_sb + (int64_t)(h0 + kHT * hh + h) * p.out_sh + d] =
                 __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
         }
-        if (rank == 0 && qd == 0 && lane < 8) {
+        if (rank == 0 && qd == 0 && lane < kHT) {
           float mh = 0.f, lh = 0.f;
 #pragma unroll
-          for (int h = 0; h < 8; ++h)
+          for (int h = 0; h < kHT; ++h)
             if (h == lane) {
               mh = M[h];
               lh = Lt[h];
             }
-          p.lse[b * p.lse_sb + (int64_t)(h0 + 8 * hh + lane) * p.lse_sh] =
+          p.lse[b * p.lse_sb + (int64_t)(h0 + kHT * hh + lane) * p.lse_sh] =
               lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
         }
         // every part has been counted and read: the counter is ready for the next call

@@ -155,12 +155,13 @@ int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream)
  * nothing (no cudaMalloc, cudaFree or allocating library routine).
  *   - The first call on a device resolves the array's device address (once per device,
  *     with that device current) and keeps it for later calls.
- *   - Limit: 8448 bytes of header and split-K counters, plus 32,896 bytes per cluster
- *     pair of the persistent grid when rows are split between pairs.  A call whose
- *     (row, 16-head group) count fits the grid (at most 74 on a 148-SM B200, e.g. 64
- *     rows of 16 heads) splits no row and always fits; a larger call runs split rows on
- *     every pair and needs 2.4 MB, beyond the array: it returns DSA_ERR_SCRATCH_LIMIT
- *     (use dsa_sparse_mla_decode).
+ *   - Limit: 8448 bytes of header and split-K counters, plus, when rows are split
+ *     between cluster pairs of the persistent grid, one partial per pair (32,896 bytes
+ *     for 16-head rows, 65,792 bytes for wider rows, which run as 32-head groups).  A
+ *     call whose (row, head group) count fits the grid (at most 74 on a 148-SM B200,
+ *     e.g. 64 rows of 16 or 32 heads) splits no row and always fits; a larger call runs
+ *     split rows on every pair and needs 2.4 MB or more, beyond the array: it returns
+ *     DSA_ERR_SCRATCH_LIMIT (use dsa_sparse_mla_decode).
  *   - Every call on a device shares the array and finds the previous call's bytes there:
  *     the call clears the first 8448 bytes (error word and split-K arrival counters;
  *     device error bits are not reported by this entry point) and always writes the
