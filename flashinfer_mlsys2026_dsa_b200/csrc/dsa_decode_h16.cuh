@@ -348,9 +348,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         nib |= (cur[e] >= 0 ? 1u : 0u) << e;
       }
-      // A group of four padding slots is not requested at all (its value rows are
-      // cleared by the softmax warps, its scores masked).
-      const bool issue = nib != 0u;
+      // In a tile with any valid slot every group is requested: a padding slot's id is
+      // out of range, so the copy fills its row with zeros, and PV reads 0 * 0 there
+      // instead of stale bytes.  An all-padding tile is not requested at all (its score
+      // and PV are skipped).  Every producer warp sees the same ids, so the same tiles.
+      const bool tile_live = __ballot_sync(0xffffffffu, nib != 0u) != 0u;
+      const bool issue = has && tile_live;
       const uint32_t n_req = (uint32_t)__popc(__ballot_sync(0xffffffffu, issue));
       uint32_t w0 = 0, w1 = 0, w2 = 0;
       if (blk == 0) {
@@ -678,17 +681,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (live && slot_ok)
                   *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(kHT * hh + h, slot & 63)) =
                       __float2bfloat16_rn(pv);
-              }
-              if (live && slot_ok && !valid) {
-                // A padded slot of a live tile: P is 0, but 0 * (stale non-finite bytes) would
-                // poison the PV sum, so clear this slot's value row (d-blocks 2hh, 2hh+1).
-                uint8_t* row = sgen + OFF_KV + st * kStageB + slot * 128;
-#pragma unroll
-                for (int jb = 0; jb < 2; ++jb)
-#pragma unroll
-                  for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(row + (2 * hh + jb) * kRB + c * 16) =
-                        make_uint4(0u, 0u, 0u, 0u);
               }
               ptx::fence_proxy_async_smem();
               ptx::tc_fence_before();

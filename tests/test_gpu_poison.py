@@ -1,9 +1,10 @@
 """Stale shared memory never reaches the output.
 
-The decode kernel does not gather the rows of padded slots (a group of four padding slots is
-not requested at all), so their shared-memory rows hold whatever the SM last stored there;
-the softmax warps clear those value rows before PV reads them, and masked scores never see
-them. These tests fill every SM's shared memory with NaN bit patterns right before each
+A padded slot's shared-memory row is written by the gather itself: its id lies outside the
+tensor map, so the copy fills the row with zeros (rows of all-padding tiles, which are
+not copied, are never read: their score and PV are skipped). If that ever stopped holding,
+the row would keep whatever the SM last stored there. These tests fill every SM's shared
+memory with NaN bit patterns right before each
 decode (a small kernel compiled at run time with NVRTC) and check that padding-heavy inputs
 still give finite outputs within tolerance of the reference, bit-identical to an unpoisoned
 run.
