@@ -413,7 +413,7 @@ int check_args(const DecodeArgs& a) {
 // Which kernel a call runs, its persistent grid and the scratch it needs.
 struct Plan {
   int nh = 16;        // heads per work unit (16 or 32)
-  int tpr = 0;        // 96-slot tiles per (row, head group)
+  int tpr = 0;        // tiles per (row, head group)
   int64_t units = 0;  // (row, group) pairs x tpr
   int grid = 0;       // cluster pairs of the persistent grid
   size_t need = 0;    // bytes of error header, counters and partials
@@ -424,7 +424,8 @@ int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
   if (cap <= 0) return DSA_ERR_CUDA;
   pl.nh = group_heads(a.num_heads);
   const int hg = a.num_heads / pl.nh;  // head groups per row
-  pl.tpr = (a.topk + h16::kTS - 1) / h16::kTS;
+  const int ts = pl.nh == 16 ? h16::Cfg<16>::kTS : h16::Cfg<32>::kTS;  // slots per tile
+  pl.tpr = (a.topk + ts - 1) / ts;
   const int64_t num_rh = a.num_tokens * hg;
   pl.units = num_rh * (int64_t)pl.tpr;
   // With no more (row, group) pairs than the grid holds, each gets a whole cluster pair and

@@ -35,15 +35,10 @@
 namespace dsa {
 namespace h16 {
 
-constexpr int kTS = 96;                  // slots per tile; the score MMA is M=128 and its
-                                         // rows >= kTS read past the region (never used)
 constexpr int kBlk = 4;                  // 64-wide ckv d-blocks per CTA
-constexpr int kRB = kTS * 128;           // one ckv d-block region of a stage
-constexpr int kRK = kTS * 64;            // the 32-wide kpe region of a stage
-constexpr int kStageB = kBlk * kRB + kRK;
 constexpr int kStages = 3;
-constexpr int kGroups = kTS / 4;         // gather4 copies per d-block per tile
-constexpr int kPVKs = kTS / 16;          // K steps of one PV MMA chain
+constexpr int kMaskStride = 8;           // mask words per stage: [0, 4) slot bits, [7] any
+constexpr int kMaskAny = 7;
 constexpr int OFF_KV = 0;
 constexpr int kThreads = 512;
 constexpr int kQWarp = 0;
@@ -64,18 +59,29 @@ constexpr uint32_t kSw128 = 2, kSw64 = 4;  // UMMA descriptor layout types
 
 // What depends on the head-group width NH (the N of both MMAs): 16 for H = 16, 32 for
 // H = 32, 64, 128 (a 128-head row is then 4 units instead of 8, each tile doing twice the
-// head work for about the same fixed cost).  With 32 heads the Q half and the exchange
-// buffer double, so Q is single-buffered (a segment's Q loads once its predecessor's
-// last score is done) and P has two buffers (softmax waits for the PV two tiles back).
+// head work for about the same fixed cost), and the tile size: the score MMA covers 128
+// slot rows whatever the tile holds, so 16-head units use 112-slot tiles (a 2048-slot row
+// is 19 tiles of 32 MMAs instead of 22 of 30); 32-head units, whose Q half and exchange
+// buffers are twice as large, keep 96.  Q is single-buffered (a segment's Q loads once its
+// predecessor's last score is done); with 32 heads P has two buffers (softmax waits for
+// the PV two tiles back).
 template <int NH>
 struct Cfg {
   static_assert(NH == 16 || NH == 32, "head group width");
+  static constexpr int kTS = NH == 16 ? 112 : 96;  // slots per tile; score MMA rows >= kTS
+                                                   // read past the region (never used)
+  static constexpr int kRB = kTS * 128;            // one ckv d-block region of a stage
+  static constexpr int kRK = kTS * 64;             // the 32-wide kpe region of a stage
+  static constexpr int kStageB = kBlk * kRB + kRK;
+  static constexpr int kGroups = kTS / 4;          // gather4 copies per d-block per tile
+  static constexpr int kPVKs = kTS / 16;           // K steps of one PV MMA chain
+  static constexpr int kMaskWords = (kTS + 31) / 32;
   static constexpr int kHT = NH / 2;               // heads per softmax thread
-  static constexpr int kQBufs = NH == 16 ? 2 : 1;
+  static constexpr int kQBufs = 1;
   static constexpr int kPBufs = NH == 16 ? kStages : 2;
-  // exchange buffers: four let softmax send tile i+1's partial before finishing tile i
-  // (see the softmax loop); with 32 heads only two fit
-  static constexpr int kXBufs = NH == 16 ? 4 : 2;
+  // exchange buffers: four would let softmax send tile i+1's partial before finishing
+  // tile i (see the softmax loop); two fit
+  static constexpr int kXBufs = 2;
   static constexpr int kQBlk = NH * 128;           // one [NH x 64] SW128 Q block
   static constexpr int kQB = kBlk * kQBlk + NH * 64;  // + the [NH x 32] SW64 q_pe block
   static constexpr int kPBlk = NH * 128;           // P^T: [NH x 64 slots] bf16 SW128 block
@@ -86,9 +92,10 @@ struct Cfg {
   static constexpr int OFF_X = OFF_P + kPBufs * kPB;
   static constexpr int OFF_BAR = OFF_X + kXBufs * kXB;
   static constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
-  static constexpr int OFF_MISC = OFF_MASK + 64;  // [0] TMEM base, [2] abort flag, [3] drain
+  static constexpr int OFF_MISC = OFF_MASK + 128;  // [0] TMEM base, [2] abort flag, [3] drain
                                                   // flag, [6] the peer's abort flag (at exit)
   static constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][kHT heads] floats
+  static_assert(kTS % 16 == 0 && kTS <= 128 && kGroups <= 32 && kMaskWords <= 4, "tile shape");
   static constexpr int SMEM_USED = OFF_RED + 2 * 4 * kHT * 4;
   static constexpr int SMEM_BYTES = SMEM_USED + 1024;
   static constexpr int TMEM_COLS = NH == 16 ? 64 : 128;
@@ -130,8 +137,7 @@ __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage
 // and the same argument gives j - 2).
 
 static_assert(B_COUNT * 8 <= 512, "barrier block");
-static_assert(kTS % 16 == 0 && kTS <= 128 && kGroups <= 32, "tile shape");
-static_assert(kStages * 4 * 4 <= 64, "mask words");
+static_assert(kStages * kMaskStride * 4 <= 128, "mask words");
 
 __device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
                                          uint32_t layout) {
@@ -142,6 +148,7 @@ __device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t 
 
 // Index entries of tile t of (row, 16-head group) rh for a producer lane's group g: slot
 // ids, or token positions in a paged call; -1 past topk.
+template <int kTS>
 __device__ __forceinline__ void tile_entries(const Params& p, int64_t rh, int t, bool has, int g,
                                              int (&r)[4]) {
   const int32_t* ir = p.idx + (rh >> p.hg_shift) * p.idx_sb;
@@ -196,6 +203,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int OFF_MASK = C::OFF_MASK, OFF_MISC = C::OFF_MISC, OFF_RED = C::OFF_RED;
   constexpr int TMEM_COLS = C::TMEM_COLS, S_COL = C::S_COL, O_COL = C::O_COL;
   constexpr int kSlotFloats = C::kSlotFloats;
+  constexpr int kTS = C::kTS, kRB = C::kRB, kStageB = C::kStageB, kGroups = C::kGroups;
+  constexpr int kPVKs = C::kPVKs;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
@@ -309,7 +318,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int n_t = (int)(u_lo - n_rh * p.tpr);
     int64_t a_rh = n_rh;  // paged: row of the positions held in `ahead`
     if (u_lo < u_hi) {
-      tile_entries(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
+      tile_entries<kTS>(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
       if constexpr (kPaged) translate(p, n_rh, ahead, cur);
     }
     if constexpr (kPaged) {
@@ -318,7 +327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ++n_rh;
       }
       a_rh = n_rh;
-      if (u_lo + 1 < u_hi) tile_entries(p, n_rh, n_t, has, g, ahead);
+      if (u_lo + 1 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, ahead);
     }
     int st = 0;
     uint32_t phase = 0;
@@ -334,9 +343,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if constexpr (kPaged) {
         a_rh = n_rh;
-        if (uu + 2 < u_hi) tile_entries(p, n_rh, n_t, has, g, ahead);
+        if (uu + 2 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, ahead);
       } else {
-        if (uu + 1 < u_hi) tile_entries(p, n_rh, n_t, has, g, nxt);
+        if (uu + 1 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, nxt);
       }
       uint32_t nib = 0;
       bool bad = false;
@@ -355,22 +364,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool tile_live = __ballot_sync(0xffffffffu, nib != 0u) != 0u;
       const bool issue = has && tile_live;
       const uint32_t n_req = (uint32_t)__popc(__ballot_sync(0xffffffffu, issue));
-      uint32_t w0 = 0, w1 = 0, w2 = 0;
+      uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
       if (blk == 0) {
         if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
         const uint32_t sh = nib << (4 * (g & 7));
         w0 = __reduce_or_sync(0xffffffffu, (g >> 3) == 0 ? sh : 0u);
         w1 = __reduce_or_sync(0xffffffffu, (g >> 3) == 1 ? sh : 0u);
         w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
+        w3 = __reduce_or_sync(0xffffffffu, (g >> 3) == 3 ? sh : 0u);
       }
       if (lane == 0) {
         ok = wait(bar(kve(st, blk)), phase ^ 1u);
         if (ok) {
           if (blk == 0) {
-            masks[st * 4 + 0] = w0;
-            masks[st * 4 + 1] = w1;
-            masks[st * 4 + 2] = w2;
-            masks[st * 4 + 3] = w0 | w1 | w2;  // nonzero: the tile has a valid slot
+            masks[st * kMaskStride + 0] = w0;
+            masks[st * kMaskStride + 1] = w1;
+            masks[st * kMaskStride + 2] = w2;
+            masks[st * kMaskStride + 3] = w3;
+            masks[st * kMaskStride + kMaskAny] = w0 | w1 | w2 | w3;  // nonzero: a valid slot
           }
           ptx::mbar_arrive_expect_tx(bar(B_KVF + st), n_req * req_bytes);
         }
@@ -422,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           // Partial S^T[128 x 16] over this CTA's 288 columns.  An all-padding tile
           // skips its MMAs (its scores are all masked).
-          if (masks[st * 4 + 3] != 0u) {
+          if (masks[st * kMaskStride + kMaskAny] != 0u) {
             ptx::tc_fence_after();
             const uint32_t d_s = tmem + (uint32_t)(S_COL + NH * sb);
             const uint64_t ko = (uint64_t)((st * kStageB) >> 4);
@@ -477,7 +488,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             o_init = false;
           }
           if (!ok) break;
-          if (masks[st * 4 + 3] != 0u) {
+          if (masks[st * kMaskStride + kMaskAny] != 0u) {
             ptx::tc_fence_after();
             const uint64_t vo = (uint64_t)((st * kStageB) >> 4);
             const uint64_t po = (uint64_t)(((int)(j % kPBufs) * kPB) >> 4);
@@ -583,8 +594,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           // ------------------------------------------------ B(ip): finish the tile in flight
           const int st = (int)(ip % kStages);
           const int xb = (int)(ip % kXBufs);
-          const uint32_t mw = qd < 3 ? masks[st * 4 + qd] : 0u;
-          const bool live = masks[st * 4 + 3] != 0u;
+          const uint32_t mw = qd < C::kMaskWords ? masks[st * kMaskStride + qd] : 0u;
+          const bool live = masks[st * kMaskStride + kMaskAny] != 0u;
           const bool valid = slot_ok && ((mw >> lane) & 1u);
             bool ok = ok_prev && wait(bar(B_XF + xb), (uint32_t)((ip / kXBufs) & 1));
             float x[kHT];
