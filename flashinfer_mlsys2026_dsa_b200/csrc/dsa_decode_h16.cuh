@@ -9,7 +9,8 @@
 // fit in one SM's shared memory.  So each CTA of the pair owns half of every slot:
 //   rank r: ckv columns [256r, 256r + 256) (four 64-wide d-blocks, 128-byte swizzle)
 //           and kpe columns [32r, 32r + 32) (one 32-wide block, 64-byte swizzle),
-// i.e. 576 bytes per slot, three 96-slot stages.  Each CTA computes a partial score
+// i.e. 576 bytes per slot, three stages of 112 (16 heads) or 96 (32 heads) slots.  Each
+// CTA computes a partial score
 // over its 288 columns; the two partials are swapped through distributed shared
 // memory and both CTAs add them (own + peer: IEEE addition commutes, so both hold
 // bit-identical scores and take identical softmax decisions).  Each CTA then runs
@@ -26,7 +27,7 @@
 //                 issuer those stalls, not the tensor core, set the tile period.
 //   warps 8-15    softmax / epilogue: warp w reads TMEM lanes 32(w%4).. (slots) and
 //                 handles heads (NH/2)((w-8)/4) .. + NH/2 - 1.
-// The work split is stream-K over (row, 96-slot tile) units per pair; a row cut between
+// The work split is stream-K over (row, tile) units per pair; a row cut between
 // pairs is merged inside this kernel by the pair holding its first tiles (per rank, for
 // its value half), after a bounded wait for the other pairs' partials.  Every wait is
 // bounded.
