@@ -714,7 +714,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------------- epilogue
       // Every thread votes here, also one that gave up after the last tile's vote.
       const int64_t il = i - 1;
-      const bool okw = !aborted && wait(bar(B_PD + (int)(il & 1)), (uint32_t)((il >> 1) & 1));
+      // PV done for tile il is a parity wait on B_PD[il & 1], which is also the barrier of
+      // tile il - 2: if PV(il - 2) were still running, that barrier would sit in the phase of
+      // the opposite parity and the wait would pass at once.  PV completes in order and
+      // PV(il - 3) is done (tile il's stage was refilled after it), so wait for PV(il - 1)
+      // first: then PV(il - 2) is done and the wait for PV(il) is exact.
+      bool okw = !aborted;
+      if (okw && il >= 1)
+        okw = wait(bar(B_PD + (int)((il - 1) & 1)), (uint32_t)(((il - 1) >> 1) & 1));
+      okw = okw && wait(bar(B_PD + (int)(il & 1)), (uint32_t)((il >> 1) & 1));
       if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !okw)) {
         aborted = true;
         break;
