@@ -176,7 +176,7 @@ def run_reference(args):
 
 # DRAM bytes (read + write) of one decode launch, from the ncu capture summarised in
 # profiles/dsa_decode_h16_b64_h16_metrics.md (dram__bytes_read.sum + dram__bytes_write.sum).
-MEASURED_TRAFFIC = {"b64_h16": 160509440}
+MEASURED_TRAFFIC = {"b64_h16": 160330496}
 
 
 def max_over_ranks(values, world, device):
