@@ -80,9 +80,7 @@ struct Cfg {
   static constexpr int kHT = NH / 2;               // heads per softmax thread
   static constexpr int kQBufs = 1;
   static constexpr int kPBufs = NH == 16 ? kStages : 2;
-  // exchange buffers: four would let softmax send tile i+1's partial before finishing
-  // tile i (see the softmax loop); two fit
-  static constexpr int kXBufs = 2;
+  static constexpr int kXBufs = 2;                 // partial-score exchange buffers
   static constexpr int kQBlk = NH * 128;           // one [NH x 64] SW128 Q block
   static constexpr int kQB = kBlk * kQBlk + NH * 64;  // + the [NH x 32] SW64 q_pe block
   static constexpr int kPBlk = NH * 128;           // P^T: [NH x 64 slots] bf16 SW128 block
@@ -122,7 +120,7 @@ enum : int {
   B_QF = B_KVE + kStages * 5, B_QE = B_QF + 2,
   B_SF = B_QE + 2, B_SE = B_SF + 2,  // score buffer full / read
   B_PF = B_SE + 2, B_PD = B_PF + 2,  // P written (+ O rescaled) / PV done
-  B_XF = B_PD + 2,               // [kXBufs <= 4] the peer's partial scores are in X[b]
+  B_XF = B_PD + 2,               // [kXBufs] the peer's partial scores are in X[b]
                                  // (complete_tx)
   B_OF = B_XF + 4,               // the epilogue has read O
   B_DRAIN = B_OF + 1,            // [2] used only when an issuer stops early
@@ -130,12 +128,9 @@ enum : int {
 };
 __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * 5 + blk; }
 // The exchange buffers X need no "empty" barrier.  A thread sends its partial of tile j
-// (into the peer's X[j % kXBufs]) only after it finished tile j - 2, whose X wait needed
-// every peer thread's partial of tile j - 2; a peer thread sends that only after it
-// finished tile j - 4 (in the look-ahead order) or j - 3 (in plain order).  So X[b] is
-// rewritten only after both sides have read it: four buffers suffice for the look-ahead
-// order, two for the plain order (a thread then sends tile j after finishing tile j - 1,
-// and the same argument gives j - 2).
+// (into the peer's X[j % 2]) only after it finished tile j - 1, whose X wait needed every
+// peer thread's partial of tile j - 1; a peer thread sends that only after it finished
+// tile j - 2.  So X[j % 2] is rewritten only after both sides have read it for tile j - 2.
 
 static_assert(B_COUNT * 8 <= 512, "barrier block");
 static_assert(kStages * kMaskStride * 4 <= 128, "mask words");
@@ -546,9 +541,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool o_valid = false;
       // Two halves per tile: A(i) reads tile i's partial scores from TMEM and sends them to
       // the peer; B(i) waits for the peer's partial, runs the online softmax and writes P.
-      // With four exchange buffers a warp whose next score is already done runs A(i+1)
-      // before B(i), so the exchange latency of tile i+1 overlaps the softmax of tile i;
-      // otherwise (or with two buffers) it runs B(i) first, as a plain sequence would.
       uint32_t own_prev[kHT];  // the in-flight tile's own partial scores
       auto fetch_send = [&](int64_t ic, uint32_t* own) -> bool {
         const int st = (int)(ic % kStages);
@@ -581,16 +573,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int64_t ip = i++;  // the tile in flight
       for (int t = s.t0 + 1;; ++t) {
         const bool more = t < s.t1;
-        uint32_t own_cur[kHT];
-        bool ok_cur = false;
-        bool a_first = false;  // A(i) before B(ip): only when the next score is done
-        if constexpr (kXBufs >= 4) {
-          if (more)
-            a_first = __all_sync(0xffffffffu,
-                                 aborted || ptx::mbar_test_wait(bar(B_SF + (int)(i & 1)),
-                                                                (uint32_t)((i >> 1) & 1)));
-          if (a_first) ok_cur = fetch_send(i, own_cur);
-        }
         {
           // ------------------------------------------------ B(ip): finish the tile in flight
           const int st = (int)(ip % kStages);
@@ -702,13 +684,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
         }
         if (!more) break;
-        if (a_first) {
-#pragma unroll
-          for (int h = 0; h < kHT; ++h) own_prev[h] = own_cur[h];
-          ok_prev = ok_cur;
-        } else {
-          ok_prev = fetch_send(i, own_prev);  // own_prev is dead after B(ip)
-        }
+        ok_prev = fetch_send(i, own_prev);  // own_prev is dead after B(ip)
         ip = i++;
       }
       // ---------------------------------------------------------------- epilogue
