@@ -7,8 +7,8 @@
 //     lse[b,h] = log2(sum_k exp(z[h,k]))
 //     out[b,h] = bf16(sum_k softmax(z)[h,k] * ckv[idx[b,k]])
 //
-// The kernel (dsa_decode_h16.cuh) runs on two-CTA clusters, one 16-head group of one row
-// per work unit; this file holds what it shares with the host side (parameters, the
+// The kernel (dsa_decode_h16.cuh) runs on two-CTA clusters, one head group (16 or 32
+// heads) of one row per work unit; this file holds what it shares with the host side (parameters, the
 // bounded wait, the stream-K split) and the C ABI of include/dsa_b200.h.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -38,10 +38,10 @@ struct Params {
   float* lse;
   int64_t lse_sb, lse_sh;
   int64_t num_slots;
-  int64_t units;  // (row, 16-head group) pairs x tpr
-  int32_t hg_shift;  // log2 of the 16-head groups per row (0, 1, 2 or 3)
+  int64_t units;  // (row, head group) pairs x tpr
+  int32_t hg_shift;  // log2 of the head groups per row (0 to 2 for 32-head groups)
   int32_t topk;
-  int32_t tpr;    // tiles per (row, 16-head group)
+  int32_t tpr;    // tiles per (row, head group)
   float scale_log2;
   uint32_t* err;
   float* parts;       // split-K partials, one slot per cluster pair
@@ -112,7 +112,7 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t G) {
 }
 
 struct Segment {
-  int64_t rh;  // (row << hg_shift) + 16-head group
+  int64_t rh;  // (row << hg_shift) + head group
   int t0, t1;  // tile range [t0, t1) within the row
 };
 

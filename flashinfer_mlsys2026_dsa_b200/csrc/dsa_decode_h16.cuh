@@ -142,7 +142,7 @@ __device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t 
          ((uint64_t)layout << 61);
 }
 
-// Index entries of tile t of (row, 16-head group) rh for a producer lane's group g: slot
+// Index entries of tile t of (row, head group) rh for a producer lane's group g: slot
 // ids, or token positions in a paged call; -1 past topk.
 template <int kTS>
 __device__ __forceinline__ void tile_entries(const Params& p, int64_t rh, int t, bool has, int g,
