@@ -532,6 +532,191 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int64_t u = u_lo;
     Segment s;
     float m_run[kHT], l_part[kHT];
+    // ---------------------------------------------------------------- epilogue
+    // A segment's output (or split-K partial / merge), from O in TMEM and the segment's
+    // running max em and sums el.  Every thread votes in it, also one that gave up earlier;
+    // returns false when the CTA gave up.
+    auto finish = [&](const Segment& es, const float (&em)[kHT], const float (&el)[kHT],
+                      int64_t eil) -> bool {
+      // PV done for tile eil is a parity wait on B_PD[eil & 1], which is also the barrier
+      // of tile eil - 2: if PV(eil - 2) were still running, that barrier would sit in the
+      // phase of the opposite parity and the wait would pass at once.  PV completes in
+      // order and PV(eil - 3) is done (tile eil's stage was refilled after it), so wait for
+      // PV(eil - 1) first: then PV(eil - 2) is done and the wait for PV(eil) is exact.
+      // (The next segment's PV cannot start before this epilogue has read O.)
+
+        bool okw = !aborted;
+        if (okw && eil >= 1)
+          okw = wait(bar(B_PD + (int)((eil - 1) & 1)), (uint32_t)(((eil - 1) >> 1) & 1));
+        okw = okw && wait(bar(B_PD + (int)(eil & 1)), (uint32_t)((eil >> 1) & 1));
+        if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !okw)) {
+          aborted = true;
+          return false;
+        }
+        ptx::tc_fence_after();
+        float* red_sum = red;  // the max slots are free again: every thread passed the vote
+#pragma unroll
+        for (int h = 0; h < kHT; ++h) {
+          float v = el[h];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+          if (lane == 0) red_sum[(hh * 4 + qd) * kHT + h] = v;
+        }
+        ptx::bar_sync(kNamedBar, kSmThreads);
+        float L[kHT];
+#pragma unroll
+        for (int h = 0; h < kHT; ++h) {
+          const float* r4 = red_sum + hh * 4 * kHT + h;
+          L[h] = (r4[0] + r4[kHT]) + (r4[2 * kHT] + r4[3 * kHT]);
+        }
+        const int64_t rh = es.rh;                        // (row, NH-head group)
+        const int64_t b = rh >> p.hg_shift;
+        const int h0 = NH * (int)(rh & ((1 << p.hg_shift) - 1));   // first head of the group
+        const bool full = (es.t0 == 0 && es.t1 == p.tpr);
+        // A row cut between pairs: the pair holding its first tiles (the head, p_lo) ends
+        // its range with them; the others start theirs with the rest and so finish early.
+        // They write their partial and count themselves; the head waits for the count and
+        // merges from its own O in TMEM, so it writes no partial and no fence delays it.
+        const int64_t p_lo = full ? pair : cta_of(rh * p.tpr, p.units, G);
+        const int64_t p_hi = full ? pair : cta_of((rh + 1) * p.tpr - 1, p.units, G);
+        const bool head = full || pair == p_lo;
+        // a pair writes a partial only for the row its range starts inside: one slot each
+        float* part = p.parts + pair * kSlotFloats;
+        float o_mine[2][kHT];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t rr[kHT];
+#pragma unroll
+          for (int c = 0; c < kHT; c += 8)
+            ptx::tmem_ld8(tmem + lane_base + (uint32_t)(O_COL + NH * mt + kHT * hh + c), rr + c);
+          ptx::tmem_wait_ld();
+          const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
+#pragma unroll
+          for (int h = 0; h < kHT; ++h) {
+            const float o = __uint_as_float(rr[h]);
+            o_mine[mt][h] = o;
+            const int head_idx = kHT * hh + h;
+            if (full)
+              p.out[b * p.out_sb + (int64_t)(h0 + head_idx) * p.out_sh + d] =
+                  __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
+            else if (!head)
+              part[head_idx * kDCkv + d] = o;
+          }
+        }
+        if (qd == 0 && lane < kHT) {
+          float mh = 0.f, lh = 0.f;  // unrolled select keeps m_run / L in registers
+#pragma unroll
+          for (int h = 0; h < kHT; ++h)
+            if (h == lane) {
+              mh = em[h];
+              lh = L[h];
+            }
+          const int head_idx = kHT * hh + lane;
+          if (full) {
+            if (rank == 0)
+              p.lse[b * p.lse_sb + (int64_t)(h0 + head_idx) * p.lse_sh] =
+                  lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+          } else if (!head) {
+            // both ranks write the (identical) scalars, so each rank's merge finds them
+            part[NH * kDCkv + head_idx] = mh;
+            part[NH * kDCkv + NH + head_idx] = lh;
+          }
+        }
+        uint32_t* cnt = p.counters + 2 * p_lo + rank;
+        if (!full && !head) {
+          // every thread's partial stores, then one release add (cumulative over the barrier)
+          ptx::bar_sync(kNamedBar, kSmThreads);
+          if (warp == kSm0 && lane == 0) ptx::red_release_gpu_add(cnt, 1u);
+        } else if (!full) {
+          if (warp == kSm0 && lane == 0) {
+            // Bounded wait for the other parts of the row (all pairs are co-resident); the
+            // acquire load orders the partial reads after it (through the barrier below).
+            const uint32_t want = (uint32_t)(p_hi - p_lo);
+            const uint64_t t0 = ptx::cycles();
+            uint32_t got = ptx::ld_acquire_gpu(cnt);
+            while (got != want) {
+              if (ptx::cycles() - t0 > kWaitCycles || misc[2]) {
+                misc[2] = 1;
+                atomicOr(p.err, (uint32_t)DSA_DEVERR_TIMEOUT);
+                break;
+              }
+              __nanosleep(32);
+              got = ptx::ld_acquire_gpu(cnt);
+            }
+          }
+          ptx::bar_sync(kNamedBar, kSmThreads);
+          float M[kHT], Lt[kHT], acc[2][kHT];
+#pragma unroll
+          for (int h = 0; h < kHT; ++h) {
+            M[h] = em[h];
+            Lt[h] = L[h];
+            acc[0][h] = o_mine[0][h];
+            acc[1][h] = o_mine[1][h];
+          }
+          for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
+            // a later pair's range starts inside this row: its partial is in its slot
+            const float* pp = p.parts + cc * kSlotFloats;
+            float pm[kHT], pl[kHT], po[2][kHT];
+            // every load of the part first, so that the part costs one L2 round trip
+#pragma unroll
+            for (int h = 0; h < kHT; ++h) {
+              const int head_idx = kHT * hh + h;
+              pm[h] = __ldcg(pp + NH * kDCkv + head_idx);
+              pl[h] = __ldcg(pp + NH * kDCkv + NH + head_idx);
+#pragma unroll
+              for (int mt = 0; mt < 2; ++mt)
+                po[mt][h] = __ldcg(pp + head_idx * kDCkv + (int)(256 * rank) + 128 * mt + 32 * qd + lane);
+            }
+#pragma unroll
+            for (int h = 0; h < kHT; ++h) {
+              // A part with l == 0 saw only padding; its O (maybe stale) is not used.
+              const bool live = pl[h] > 0.f;
+              const bool have = Lt[h] > 0.f;
+              const float mn = !live ? M[h] : (!have ? pm[h] : fmaxf(M[h], pm[h]));
+              const float keep = have ? ptx::ex2(M[h] - mn) : 0.f;
+              const float w = live ? ptx::ex2(pm[h] - mn) : 0.f;
+              Lt[h] = (have ? Lt[h] * keep : 0.f) + (live ? w * pl[h] : 0.f);
+#pragma unroll
+              for (int mt = 0; mt < 2; ++mt)
+                acc[mt][h] = (have ? acc[mt][h] * keep : 0.f) + (live ? w * po[mt][h] : 0.f);
+              M[h] = mn;
+            }
+          }
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
+#pragma unroll
+            for (int h = 0; h < kHT; ++h)
+              p.out[b * p.out_sb + (int64_t)(h0 + kHT * hh + h) * p.out_sh + d] =
+                  __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
+          }
+          if (rank == 0 && qd == 0 && lane < kHT) {
+            float mh = 0.f, lh = 0.f;
+#pragma unroll
+            for (int h = 0; h < kHT; ++h)
+              if (h == lane) {
+                mh = M[h];
+                lh = Lt[h];
+              }
+            p.lse[b * p.lse_sb + (int64_t)(h0 + kHT * hh + lane) * p.lse_sh] =
+                lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+          }
+          // every part has been counted and read: the counter is ready for the next call
+          if (warp == kSm0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(B_OF));
+      return true;
+    };
+    // 16-head units run a segment's epilogue one tile into the next segment, so the
+    // segment's last PVs have drained by then instead of being waited for (with 32 heads
+    // the saved sums would not fit the softmax warps' registers)
+    constexpr bool kDefer = NH == 16;
+    bool pending = false;
+    Segment ps;
+    float pm_run[kHT], pl_part[kHT];
+    int64_t pil = 0;
     while (!aborted && next_segment(u, u_hi, p.tpr, s)) {
 #pragma unroll
       for (int h = 0; h < kHT; ++h) {
@@ -683,182 +868,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               o_valid = o_valid || live;
             }
         }
+        if (pending) {  // the previous segment's epilogue, now that its PVs have drained
+          pending = false;
+          if (!finish(ps, pm_run, pl_part, pil)) break;
+        }
         if (!more) break;
         ok_prev = fetch_send(i, own_prev);  // own_prev is dead after B(ip)
         ip = i++;
       }
-      // ---------------------------------------------------------------- epilogue
-      // Every thread votes here, also one that gave up after the last tile's vote.
-      const int64_t il = i - 1;
-      // PV done for tile il is a parity wait on B_PD[il & 1], which is also the barrier of
-      // tile il - 2: if PV(il - 2) were still running, that barrier would sit in the phase of
-      // the opposite parity and the wait would pass at once.  PV completes in order and
-      // PV(il - 3) is done (tile il's stage was refilled after it), so wait for PV(il - 1)
-      // first: then PV(il - 2) is done and the wait for PV(il) is exact.
-      bool okw = !aborted;
-      if (okw && il >= 1)
-        okw = wait(bar(B_PD + (int)((il - 1) & 1)), (uint32_t)(((il - 1) >> 1) & 1));
-      okw = okw && wait(bar(B_PD + (int)(il & 1)), (uint32_t)((il >> 1) & 1));
-      if (ptx::bar_red_or(kNamedBar, kSmThreads, aborted || !okw)) {
-        aborted = true;
-        break;
-      }
-      ptx::tc_fence_after();
-      float* red_sum = red;  // the max slots are free again: every thread passed the vote
-#pragma unroll
-      for (int h = 0; h < kHT; ++h) {
-        float v = l_part[h];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) red_sum[(hh * 4 + qd) * kHT + h] = v;
-      }
-      ptx::bar_sync(kNamedBar, kSmThreads);
-      float L[kHT];
-#pragma unroll
-      for (int h = 0; h < kHT; ++h) {
-        const float* r4 = red_sum + hh * 4 * kHT + h;
-        L[h] = (r4[0] + r4[kHT]) + (r4[2 * kHT] + r4[3 * kHT]);
-      }
-      const int64_t rh = s.rh;                        // (row, NH-head group)
-      const int64_t b = rh >> p.hg_shift;
-      const int h0 = NH * (int)(rh & ((1 << p.hg_shift) - 1));   // first head of the group
-      const bool full = (s.t0 == 0 && s.t1 == p.tpr);
-      // A row cut between pairs: the pair holding its first tiles (the head, p_lo) ends
-      // its range with them; the others start theirs with the rest and so finish early.
-      // They write their partial and count themselves; the head waits for the count and
-      // merges from its own O in TMEM, so it writes no partial and no fence delays it.
-      const int64_t p_lo = full ? pair : cta_of(rh * p.tpr, p.units, G);
-      const int64_t p_hi = full ? pair : cta_of((rh + 1) * p.tpr - 1, p.units, G);
-      const bool head = full || pair == p_lo;
-      // a pair writes a partial only for the row its range starts inside: one slot each
-      float* part = p.parts + pair * kSlotFloats;
-      float o_mine[2][kHT];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        uint32_t rr[kHT];
-#pragma unroll
-        for (int c = 0; c < kHT; c += 8)
-          ptx::tmem_ld8(tmem + lane_base + (uint32_t)(O_COL + NH * mt + kHT * hh + c), rr + c);
-        ptx::tmem_wait_ld();
-        const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
+      if (aborted) break;
+      if constexpr (kDefer) {
+        ps = s;
 #pragma unroll
         for (int h = 0; h < kHT; ++h) {
-          const float o = __uint_as_float(rr[h]);
-          o_mine[mt][h] = o;
-          const int head_idx = kHT * hh + h;
-          if (full)
-            p.out[b * p.out_sb + (int64_t)(h0 + head_idx) * p.out_sh + d] =
-                __float2bfloat16_rn(L[h] > 0.f ? o / L[h] : 0.f);
-          else if (!head)
-            part[head_idx * kDCkv + d] = o;
+          pm_run[h] = m_run[h];
+          pl_part[h] = l_part[h];
         }
+        pil = i - 1;
+        pending = true;
+      } else {
+        if (!finish(s, m_run, l_part, i - 1)) break;
       }
-      if (qd == 0 && lane < kHT) {
-        float mh = 0.f, lh = 0.f;  // unrolled select keeps m_run / L in registers
-#pragma unroll
-        for (int h = 0; h < kHT; ++h)
-          if (h == lane) {
-            mh = m_run[h];
-            lh = L[h];
-          }
-        const int head_idx = kHT * hh + lane;
-        if (full) {
-          if (rank == 0)
-            p.lse[b * p.lse_sb + (int64_t)(h0 + head_idx) * p.lse_sh] =
-                lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
-        } else if (!head) {
-          // both ranks write the (identical) scalars, so each rank's merge finds them
-          part[NH * kDCkv + head_idx] = mh;
-          part[NH * kDCkv + NH + head_idx] = lh;
-        }
-      }
-      uint32_t* cnt = p.counters + 2 * p_lo + rank;
-      if (!full && !head) {
-        // every thread's partial stores, then one release add (cumulative over the barrier)
-        ptx::bar_sync(kNamedBar, kSmThreads);
-        if (warp == kSm0 && lane == 0) ptx::red_release_gpu_add(cnt, 1u);
-      } else if (!full) {
-        if (warp == kSm0 && lane == 0) {
-          // Bounded wait for the other parts of the row (all pairs are co-resident); the
-          // acquire load orders the partial reads after it (through the barrier below).
-          const uint32_t want = (uint32_t)(p_hi - p_lo);
-          const uint64_t t0 = ptx::cycles();
-          uint32_t got = ptx::ld_acquire_gpu(cnt);
-          while (got != want) {
-            if (ptx::cycles() - t0 > kWaitCycles || misc[2]) {
-              misc[2] = 1;
-              atomicOr(p.err, (uint32_t)DSA_DEVERR_TIMEOUT);
-              break;
-            }
-            __nanosleep(32);
-            got = ptx::ld_acquire_gpu(cnt);
-          }
-        }
-        ptx::bar_sync(kNamedBar, kSmThreads);
-        float M[kHT], Lt[kHT], acc[2][kHT];
-#pragma unroll
-        for (int h = 0; h < kHT; ++h) {
-          M[h] = m_run[h];
-          Lt[h] = L[h];
-          acc[0][h] = o_mine[0][h];
-          acc[1][h] = o_mine[1][h];
-        }
-        for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
-          // a later pair's range starts inside this row: its partial is in its slot
-          const float* pp = p.parts + cc * kSlotFloats;
-          float pm[kHT], pl[kHT], po[2][kHT];
-          // every load of the part first, so that the part costs one L2 round trip
-#pragma unroll
-          for (int h = 0; h < kHT; ++h) {
-            const int head_idx = kHT * hh + h;
-            pm[h] = __ldcg(pp + NH * kDCkv + head_idx);
-            pl[h] = __ldcg(pp + NH * kDCkv + NH + head_idx);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-              po[mt][h] = __ldcg(pp + head_idx * kDCkv + (int)(256 * rank) + 128 * mt + 32 * qd + lane);
-          }
-#pragma unroll
-          for (int h = 0; h < kHT; ++h) {
-            // A part with l == 0 saw only padding; its O (maybe stale) is not used.
-            const bool live = pl[h] > 0.f;
-            const bool have = Lt[h] > 0.f;
-            const float mn = !live ? M[h] : (!have ? pm[h] : fmaxf(M[h], pm[h]));
-            const float keep = have ? ptx::ex2(M[h] - mn) : 0.f;
-            const float w = live ? ptx::ex2(pm[h] - mn) : 0.f;
-            Lt[h] = (have ? Lt[h] * keep : 0.f) + (live ? w * pl[h] : 0.f);
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-              acc[mt][h] = (have ? acc[mt][h] * keep : 0.f) + (live ? w * po[mt][h] : 0.f);
-            M[h] = mn;
-          }
-        }
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const int d = (int)(256 * rank) + 128 * mt + 32 * qd + lane;
-#pragma unroll
-          for (int h = 0; h < kHT; ++h)
-            p.out[b * p.out_sb + (int64_t)(h0 + kHT * hh + h) * p.out_sh + d] =
-                __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
-        }
-        if (rank == 0 && qd == 0 && lane < kHT) {
-          float mh = 0.f, lh = 0.f;
-#pragma unroll
-          for (int h = 0; h < kHT; ++h)
-            if (h == lane) {
-              mh = M[h];
-              lh = Lt[h];
-            }
-          p.lse[b * p.lse_sb + (int64_t)(h0 + kHT * hh + lane) * p.lse_sh] =
-              lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
-        }
-        // every part has been counted and read: the counter is ready for the next call
-        if (warp == kSm0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar(B_OF));
-      // The sums are read; the next segment may reuse the slots after its first vote.
     }
+    if (pending && !aborted) finish(ps, pm_run, pl_part, pil);
   }
 
   ptx::tc_fence_before();
