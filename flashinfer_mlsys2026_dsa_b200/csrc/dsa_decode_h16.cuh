@@ -313,6 +313,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int64_t n_rh = u_lo / p.tpr;
     int n_t = (int)(u_lo - n_rh * p.tpr);
     int64_t a_rh = n_rh;  // paged: row of the positions held in `ahead`
+    // paged: pull a row's page table into L2 when the producers reach the row (d-block 0's
+    // warp; 128-byte lines), so the translations read it from L2
+    auto pf_row = [&](int64_t rh) {
+      if constexpr (kPaged) {
+        if (blk != 0) return;
+        const int32_t* pr = p.pt + (rh >> p.hg_shift) * p.pt_sb;
+        for (int c = lane * 32; c < p.pt_cols; c += 32 * 32)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(pr + c));
+      }
+    };
+    if (u_lo < u_hi) pf_row(n_rh);
     if (u_lo < u_hi) {
       tile_entries<kTS>(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
       if constexpr (kPaged) translate(p, n_rh, ahead, cur);
@@ -336,6 +347,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (++n_t == p.tpr) {
         n_t = 0;
         ++n_rh;
+        if (uu + 2 < u_hi) pf_row(n_rh);
       }
       if constexpr (kPaged) {
         a_rh = n_rh;
