@@ -15,8 +15,18 @@ Reported numbers:
   e2e        the same metric through the public entry point with host buffers: per step
              the step's q_nope, q_pe and sparse_indices are copied from pinned host memory,
              the decode runs, and output + lse are copied back (the paged KV pool is
-             device-resident state, like a serving engine's cache).
-  roofline   achieved GB/s of the decode call vs the measured HBM peak.
+             device-resident state, like a serving engine's cache).  Also reported: the
+             host time spent issuing a step and the time of the step's copies alone.
+  roofline   achieved GB/s of the decode call vs the measured HBM peak; `traffic` is the
+             DRAM bytes of one call from the ncu capture recorded in
+             profiles/dram_traffic.json, reported only while the kernel sources still
+             match the capture's digest.
+  workloads  (one GPU) the other single-GPU configurations: b32_h128 (128 heads, with its
+             tensor-pipe rate) and ragged_b256 (-1 padding), timed like `value`.
+  b2048      (every N) the batch-sharded decode of a global batch of 2048 rows: each rank
+             decodes its 2048/N rows against its own page pool, at most 1024 rows per
+             call (a rank with more runs its rows as consecutive calls); per-GPU and
+             aggregate us per global batch and HBM fraction (strong scaling).
   cpu_baseline  the CPU oracle (C restatement of solution/triton/baseline.py) on a
              bounded sample of the same workload, all host cores.
 
@@ -43,13 +53,44 @@ N_SETS = 4
 
 
 def _peaks():
+    """Measured HBM copy bandwidth (GB/s) and dense bf16 rate (TFLOP/s, burst) of this pool."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        return {"hbm": float(d["hbm_gbs"]), "bf16": float(d["bf16_tflops"]), "source": "measured"}
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm": 6650.0, "bf16": 1590.0, "source": "fallback"}
+
+
+def kernel_digest() -> str:
+    """SHA-256 (16 hex digits) of the CUDA sources the decode kernel is built from."""
+    import hashlib
+
+    csrc = os.path.join(ROOT, "flashinfer_mlsys2026_dsa_b200", "csrc")
+    h = hashlib.sha256()
+    for name in sorted(os.listdir(csrc)):
+        if name.endswith((".cu", ".cuh")) and name != "kernel.cu":
+            with open(os.path.join(csrc, name), "rb") as f:
+                h.update(name.encode() + b"\0" + f.read())
+    return h.hexdigest()[:16]
+
+
+def measured_traffic(workload: str):
+    """DRAM bytes (read + write) of one call of `workload` from the committed ncu capture.
+
+    profiles/dram_traffic.json records, per workload, the bytes of one captured launch and
+    the digest of the kernel sources it was captured on; a capture of other sources is not
+    this kernel's traffic, so it is reported as None with the reason.
+    """
+    try:
+        with open(os.path.join(ROOT, "profiles", "dram_traffic.json")) as f:
+            rec = json.load(f)["workloads"][workload]
+    except (OSError, KeyError, ValueError):
+        return None, "no ncu capture of this workload"
+    if rec.get("kernel_digest") != kernel_digest():
+        return None, "the ncu capture predates the current kernel sources"
+    return int(rec["bytes_per_call"]), rec.get("profile", "")
 
 
 class ClockSampler:
@@ -160,23 +201,32 @@ def run_reference(args):
         return
     base = cpu_baseline(args.workload, args.cpu_rows, args.seed)
     from flashinfer_mlsys2026_dsa_b200 import workloads
-    B = workloads.CONFIGS[args.workload]["B"] if args.workload != "b2048" else 2048 // args.gpus
-    ms_full = base["ms_per_call"] * B / args.cpu_rows  # rows are independent
+    # The whole job of the GPU arm: `rows_per_rank` rows on each of the N ranks (b2048: the
+    # global 2048 rows).  The host's cores run it all, so its time is the per-row time of
+    # the sample times every row of the job; GB/s stays per byte, as in the GPU arm.
+    rows_per_rank = (workloads.CONFIGS[args.workload]["B"] if args.workload != "b2048"
+                     else 2048 // args.gpus)
+    job_rows = rows_per_rank * world
+    ms_full = base["ms_per_call"] * job_rows / args.cpu_rows  # rows are independent
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_full, 3), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(ms_full, 3), "higher_is_better": True,
+            "scaling": "weak" if args.workload != "b2048" else "strong",
             "vs_baseline": None, "dtype": "bf16 in, fp32 math", "data": "synthetic",
-            "config": {"workload": args.workload, "rows_per_rank": B, "heads": 16, "topk": 2048,
-                       "page_size": 64, "sample_rows": args.cpu_rows},
+            "config": {"workload": args.workload, "rows_per_rank": rows_per_rank,
+                       "job_rows": job_rows, "heads": workloads.CONFIGS[args.workload]["H"],
+                       "topk": workloads.CONFIGS[args.workload]["topk"], "page_size": 64,
+                       "sample_rows": args.cpu_rows,
+                       "basis": "whole job on all host cores: value is job bytes / job time, "
+                                "the same basis as the GPU arm's value; the host's cores do "
+                                "not grow with N"},
             "cpu_baseline": {k: v for k, v in base.items() if k != "ms_per_call"},
+            "gpu_reference": "unmeasured: the reference's Triton kernel (solution/triton/"
+                             "fused.py) needs its sources, which are not present on the GPU "
+                             "host",
             "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
-
-
-# DRAM bytes (read + write) of one decode launch, from the ncu capture summarised in
-# profiles/dsa_decode_h16_b64_h16_metrics.md (dram__bytes_read.sum + dram__bytes_write.sum).
-MEASURED_TRAFFIC = {"b64_h16": 160330496}
 
 
 def max_over_ranks(values, world, device):
@@ -190,9 +240,140 @@ def max_over_ranks(values, world, device):
     return t.tolist()
 
 
+def sum_over_ranks(values, world, device):
+    """Element-wise sum of per-rank values over all ranks of the default group."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.tolist()
+
+
 def job_gbs(bytes_per_step, steps, world, max_ms):
     """Whole-job throughput: the bytes of every rank's steps over the slowest rank's time."""
     return bytes_per_step * steps * world / (max_ms * 1e-3) / 1e9
+
+
+def graph_ms(calls, reps, warmup, stream, barrier=lambda: None):
+    """Device ms per call: CUDA-graph replays of `calls` (each replay runs each call once),
+    timed with CUDA events on the launching stream after `warmup` replays."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for c in calls:
+            c()  # eager first: allocates the stream's workspace outside the capture
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for c in calls:
+                c()
+        for _ in range(warmup):
+            g.replay()
+        stream.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        stream.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(calls))
+    del g
+    return ms
+
+
+def roofline_record(nbytes, nflops, ms, peaks, traffic_of):
+    """HBM (and tensor-pipe) roofline of one call of `nbytes` / `nflops` taking `ms`."""
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    traffic, note = traffic_of
+    rec = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
+           "frac": round(gbs / peaks["hbm"], 4), "traffic": traffic,
+           "peak_source": peaks["source"], "algorithmic_bytes_per_call": int(nbytes)}
+    if traffic is None:
+        rec["traffic_note"] = note
+    tflops = nflops / (ms * 1e-3) / 1e12
+    tensor = {"achieved_tflops": round(tflops, 1), "peak_tflops": peaks["bf16"],
+              "frac": round(tflops / peaks["bf16"], 4), "algorithmic_flops_per_call": int(nflops)}
+    return rec, tensor
+
+
+def workload_record(name, dev, stream, args, peaks, kernel, read_device_errors):
+    """One GPU, one configuration: four rotating input sets, graph-replayed like `value`."""
+    import torch
+
+    from flashinfer_mlsys2026_dsa_b200 import workloads
+
+    sets = [workloads.make(name, device=dev, seed=args.seed * 97 + s) for s in range(N_SETS)]
+    B, H = sets[0].num_tokens, sets[0].num_heads
+    out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+    calls = [lambda w=w: kernel(*w.args(), out, lse) for w in sets]
+    reps = max(1, math.ceil(args.steps / N_SETS))
+    ms = graph_ms(calls, reps, max(1, math.ceil(args.warmup / N_SETS)), stream)
+    nbytes = sum(w.algorithmic_bytes() for w in sets) / N_SETS
+    nflops = sum(w.algorithmic_flops() for w in sets) / N_SETS
+    roof, tensor = roofline_record(nbytes, nflops, ms, peaks, measured_traffic(name))
+    rec = {"us_per_call": round(ms * 1e3, 2), "value": roof["achieved"], "unit": "GB/s",
+           "rows": B, "heads": H, "topk": sets[0].topk, "roofline": roof, "tensor": tensor,
+           "tokens_per_s": round(B / (ms * 1e-3), 1),
+           "l2": f"{N_SETS} rotating input sets of {nbytes / 1e6:.0f} MB each"}
+    with torch.cuda.stream(stream):
+        rec["device_errors"] = read_device_errors(dev)
+    del sets, calls, out, lse
+    torch.cuda.empty_cache()
+    return rec
+
+
+B2048_MAX_ROWS_PER_CALL = 1024  # a 1024-row shard's page pool is about 82 GB
+
+
+def b2048_record(dev, stream, args, peaks, kernel, world, rank, barrier):
+    """The global 2048-row batch sharded over the ranks (strong scaling).
+
+    Rank r decodes rows [r * 2048/N, (r + 1) * 2048/N), each rank with its own page pool,
+    in calls of at most 1024 rows: one call per rank from 2 GPUs up, two consecutive calls
+    on one GPU (whose single pool would not fit beside the other buffers).  Rows are
+    independent, so a rank's time for the global batch is the sum of its calls' times.
+    The generator's piece index is rank * calls + call, so the same seed splits the same
+    2048 rows across ranks and calls.
+    """
+    import torch
+
+    from flashinfer_mlsys2026_dsa_b200 import workloads
+
+    rows = 2048 // world
+    calls = max(1, -(-rows // B2048_MAX_ROWS_PER_CALL))
+    reps = max(3, args.steps)
+    t_ms, nbytes, nflops = 0.0, 0.0, 0.0
+    for c in range(calls):
+        w = workloads.make("b2048", device=dev, seed=args.seed, rank=rank * calls + c,
+                           world_size=world * calls)
+        out = torch.empty(w.num_tokens, 16, 512, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(w.num_tokens, 16, dtype=torch.float32, device=dev)
+        t_ms += graph_ms([lambda: kernel(*w.args(), out, lse)], reps, args.warmup, stream,
+                         barrier)
+        nbytes += w.algorithmic_bytes()
+        nflops += w.algorithmic_flops()
+        del w, out, lse
+        torch.cuda.empty_cache()
+    t_max, = max_over_ranks([t_ms], world, dev)
+    job_bytes, = sum_over_ranks([nbytes], world, dev)
+    per_gpu_gbs = job_bytes / world / (t_max * 1e-3) / 1e9
+    return {
+        "global_batch": 2048, "rows_per_rank": rows, "calls_per_rank": calls,
+        "us_per_global_batch": round(t_max * 1e3, 2),
+        "per_gpu": {"us": round(t_max * 1e3, 2), "value": round(per_gpu_gbs, 1), "unit": "GB/s",
+                    "hbm_frac": round(per_gpu_gbs / peaks["hbm"], 4),
+                    "basis": "the slowest rank's time for its rows; bytes per rank"},
+        "aggregate": {"value": round(job_bytes / (t_max * 1e-3) / 1e9, 1), "unit": "GB/s",
+                      "tokens_per_s": round(2048 / (t_max * 1e-3), 1),
+                      "algorithmic_bytes": int(job_bytes)},
+        "scaling": "strong", "n_gpus": world,
+        "timing": f"per call: CUDA-graph replay x{reps}, CUDA events, max over ranks",
+    }
 
 
 def run_ours(args):
@@ -213,6 +394,7 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
+    peaks = _peaks()
     wl_world = world if args.workload == "b2048" else 1
     sets = [workloads.make(args.workload, device=dev, seed=args.seed * 97 + s, rank=rank,
                            world_size=wl_world) for s in range(N_SETS)]
@@ -220,6 +402,7 @@ def run_ours(args):
     # kernels of this library per call: one (the cluster kernel merges split rows itself)
     launches_per_call = 1
     bytes_per_step = sum(w.algorithmic_bytes() for w in sets) / N_SETS
+    flops_per_step = sum(w.algorithmic_flops() for w in sets) / N_SETS
     out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, H, dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(device=dev)
@@ -255,35 +438,18 @@ def run_ours(args):
             e1.record(stream)
             stream.synchronize()
         torch.cuda.synchronize(dev)
+        err = read_device_errors(dev)
     dev_ms = e0.elapsed_time(e1)
-    err = read_device_errors(dev)
+    del graph
 
     # ---------------- the same steps through the paged entry (positions + page tables;
     # the slot ids are formed inside the kernel), device-timed the same way
+    pargs = [(w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, w.page_table, w.positions,
+              w.sm_scale) for w in sets]
+    paged_ms = graph_ms([lambda a=a: kernel_paged(*a, out, lse) for a in pargs], reps,
+                        max(1, math.ceil(args.warmup / N_SETS)), stream, barrier) * N_SETS * reps
     with torch.cuda.stream(stream):
-        pargs = [(w.q_nope, w.q_pe, w.ckv_cache, w.kpe_cache, w.page_table, w.positions,
-                  w.sm_scale) for w in sets]
-        for a in pargs:
-            kernel_paged(*a, out, lse)
-        stream.synchronize()
-        pgraph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(pgraph, stream=stream):
-            for a in pargs:
-                kernel_paged(*a, out, lse)
-        for _ in range(max(1, math.ceil(args.warmup / N_SETS))):
-            pgraph.replay()
-        stream.synchronize()
-        barrier()
-        p0 = torch.cuda.Event(enable_timing=True)
-        p1 = torch.cuda.Event(enable_timing=True)
-        p0.record(stream)
-        for _ in range(reps):
-            pgraph.replay()
-        p1.record(stream)
-        stream.synchronize()
-    paged_ms = p0.elapsed_time(p1)
-    err |= read_device_errors(dev)
-    del pgraph
+        err |= read_device_errors(dev)
 
     # ---------------- end to end through the public API, host buffers
     # Every step copies its query and index rows from pinned host memory, runs the public
@@ -356,21 +522,51 @@ def run_ours(args):
     f0.record(s_in)
     s_run.wait_event(f0)
     s_out.wait_event(f0)
+    h0 = time.perf_counter()
     for k in range(steps):
         e2e_step(k)
+    host_us = (time.perf_counter() - h0) / steps * 1e6
     s_in.wait_event(out_done[(steps - 1) % NSLOT])
     f1.record(s_in)
     f1.synchronize()
     e2e_ms = f0.elapsed_time(f1)
     # the last step's results really are on the host
     assert torch.isfinite(host_out[(steps - 1) % NSLOT][1][1]).any()
+    # the step's copies alone, back to back on one stream (what bounds e2e when the decode
+    # is hidden under them)
+    copy_us = {}
+    for name, (dst, src) in {"h2d": (dev_in[0][0], host_in[0]),
+                             "d2h": (host_out[0][0], dev_out[0][0])}.items():
+        torch.cuda.synchronize(dev)
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record(s_in)
+        with torch.cuda.stream(s_in):
+            for _ in range(steps):
+                dst.copy_(src, non_blocking=True)
+        c1.record(s_in)
+        c1.synchronize()
+        copy_us[name] = c0.elapsed_time(c1) / steps * 1e3
 
     dev_ms, e2e_ms, paged_ms = max_over_ranks([dev_ms, e2e_ms, paged_ms], world, dev)
     ms_per_step = dev_ms / steps
     value, e2e_value = job_gbs(bytes_per_step, steps, world, dev_ms), job_gbs(
         bytes_per_step, steps, world, e2e_ms)
-    peak, peak_kind = _peaks()
     per_call_gbs = bytes_per_step / (ms_per_step * 1e-3) / 1e9
+    roof, tensor = roofline_record(bytes_per_step, flops_per_step, ms_per_step, peaks,
+                                   measured_traffic(args.workload))
+    del sets, host_in, dev_in, dev_out, host_out, out, lse
+    torch.cuda.empty_cache()
+
+    # ---------------- the other configurations (one GPU) and the global 2048-row batch
+    extra = {}
+    if world == 1 and not args.no_extra:
+        for name in ("b32_h128", "ragged_b256"):
+            if name != args.workload:
+                extra[name] = workload_record(name, dev, stream, args, peaks, kernel,
+                                              read_device_errors)
+    b2048 = None if args.no_extra else b2048_record(dev, stream, args, peaks, kernel, world,
+                                                    rank, barrier)
 
     base = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -378,7 +574,6 @@ def run_ours(args):
         base.pop("ms_per_call", None)
     if world > 1:
         dist.barrier()
-        del graph
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -387,20 +582,21 @@ def run_ours(args):
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
         "us_per_call": round(ms_per_step * 1e3, 2),
         "tokens_per_s": round(B * world / (ms_per_step * 1e-3), 1),
-        "hbm_frac_of_measured": round(per_call_gbs / peak, 4),
+        "hbm_frac_of_measured": round(per_call_gbs / peaks["hbm"], 4),
         "hbm_frac_of_nominal_8tbs": round(per_call_gbs / 8000.0, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
         "config": {"workload": args.workload, "rows_per_rank": B, "heads": H,
-                   "topk": sets[0].topk, "page_size": 64, "parallelism": f"batch-sharded x{world}",
+                   "topk": workloads.CONFIGS[args.workload]["topk"],
+                   "page_size": 64, "parallelism": f"batch-sharded x{world}",
                    "l2": f"{N_SETS} rotating input sets of {bytes_per_step / 1e6:.0f} MB each "
                          f"(> 126 MB L2)", "timing": "CUDA graph replay, CUDA events"},
-        "roofline": {"bound": "hbm", "achieved": round(per_call_gbs, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(per_call_gbs / peak, 4),
-                     "traffic": MEASURED_TRAFFIC.get(args.workload), "peak_source": peak_kind,
-                     "algorithmic_bytes_per_call": int(bytes_per_step)},
+        "roofline": roof,
+        "tensor": tensor,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 4),
+                "host_us_per_step": round(host_us, 1),
+                "h2d_copy_us": round(copy_us["h2d"], 1), "d2h_copy_us": round(copy_us["d2h"], 1),
                 "method": "public kernel() per step; one pinned H2D copy of the step's q_nope, "
                           "q_pe, indices and one D2H copy of its out, lse inside the timed "
                           "region; copies and decode on three streams with two buffer slots "
@@ -414,6 +610,10 @@ def run_ours(args):
         "clocks": clk.summary(),
         "device_errors": err,
     }
+    if extra:
+        line["workloads"] = extra
+    if b2048 is not None:
+        line["b2048"] = b2048
     if base is not None:
         line["cpu_baseline"] = base
     print(json.dumps(line), flush=True)
@@ -432,6 +632,8 @@ def main():
                     help="decode rows in the CPU-baseline sample (default: one per host core, "
                          "at most the workload's rows)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other configurations and the 2048-row batch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

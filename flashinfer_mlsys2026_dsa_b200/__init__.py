@@ -5,7 +5,9 @@ Drop-in for the reference solution's entry point
 (Dogacel/flashinfer-mlsys2026-dsa, solution/triton/fused.py:150), backed by one
 hand-written sm_100a CUDA kernel reached through the C ABI in include/dsa_b200.h.
 """
-from .ops import DSAError, decode, kernel, kernel_paged, read_device_errors, workspace_for  # noqa: F401
+from .ops import (DSAError, decode, kernel, kernel_paged, read_device_errors,  # noqa: F401
+                  set_strict, workspace_for)
 
-__all__ = ["kernel", "kernel_paged", "decode", "read_device_errors", "workspace_for", "DSAError"]
+__all__ = ["kernel", "kernel_paged", "decode", "read_device_errors", "set_strict",
+           "workspace_for", "DSAError"]
 __version__ = "0.1.0"

@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "dsa_sparse_mla_decode_workspace_size",
     "dsa_read_error_word",
     "dsa_selftest_bounded_wait",
+    "dsa_set_wait_limit",
     "dsa_status_string",
     "dsa_abi_version",
 )
@@ -88,6 +89,8 @@ def load(build_if_missing: bool = True):
         lib.dsa_read_error_word.restype = _c.c_int
         lib.dsa_read_error_word.argtypes = [_c.c_void_p, _c.c_void_p, _c.c_int,
                                             _c.POINTER(_c.c_uint32)]
+        lib.dsa_set_wait_limit.restype = _c.c_uint64
+        lib.dsa_set_wait_limit.argtypes = [_c.c_uint64]
         lib.dsa_selftest_bounded_wait.restype = _c.c_int
         lib.dsa_selftest_bounded_wait.argtypes = [_c.c_int64, _c.c_void_p, _c.c_void_p]
         lib.dsa_status_string.restype = _c.c_char_p

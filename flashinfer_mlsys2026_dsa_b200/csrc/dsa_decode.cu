@@ -16,6 +16,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <utility>
 
@@ -28,7 +29,7 @@ constexpr int kDCkv = 512;            // latent (value) width
 constexpr int kDKpe = 64;             // rope key width
 constexpr float kTau = 8.0f;          // lazy-rescale threshold (log2 units)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint64_t kWaitCycles = 4000000000ull;  // ~2 s at the B200's ~2 GHz SM clock
+constexpr uint64_t kWaitCycles = 4000000000ull;  // default wait bound: ~2 s at ~2 GHz
 
 struct Params {
   const int32_t* idx;
@@ -46,6 +47,7 @@ struct Params {
   uint32_t* err;
   float* parts;       // split-K partials, one slot per cluster pair
   uint32_t* counters;  // split-K arrival counters, zero between calls
+  uint64_t wait_cycles;  // bound of every wait in the kernel (SM cycles)
   // paged calls only: idx holds token positions; page_table rows of pt_cols page ids
   const int32_t* pt;
   int64_t pt_sb;
@@ -81,6 +83,7 @@ __device__ __forceinline__ uint32_t sw128_off(int h, int k) {
 struct Waiter {
   volatile uint32_t* abort_flag;
   uint32_t* err;
+  uint64_t limit;  // cycles
   bool spin = false;
   __device__ __forceinline__ bool poll(uint32_t bar, uint32_t parity) const {
     return spin ? ptx::mbar_test_wait(bar, parity) : ptx::mbar_try_wait(bar, parity);
@@ -92,7 +95,7 @@ struct Waiter {
       if (poll(bar, parity)) return true;
       if ((it & 63u) == 0) {
         if (*abort_flag) return false;
-        if (ptx::cycles() - t0 > kWaitCycles) {
+        if (ptx::cycles() - t0 > limit) {
           *abort_flag = 1;
           atomicOr(err, (uint32_t)DSA_DEVERR_TIMEOUT);
           return false;
@@ -177,6 +180,9 @@ EncodeTiledFn get_encode_fn() {
 }
 
 constexpr int kMaxDevices = 64;
+
+// Bound of every wait in the kernels, in SM cycles (dsa_set_wait_limit).
+std::atomic<uint64_t> g_wait_cycles{kWaitCycles};
 
 struct DeviceState {
   int sms = 0;
@@ -494,6 +500,7 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   prm.err = reinterpret_cast<uint32_t*>(ws);
   prm.parts = reinterpret_cast<float*>(ws + kPartsOff);
   prm.counters = reinterpret_cast<uint32_t*>(ws + kCountersOff);
+  prm.wait_cycles = g_wait_cycles.load(std::memory_order_relaxed);
   prm.pt = a.page_table;
   prm.pt_sb = a.pt_sb;
   prm.pt_cols = a.pt_cols;
@@ -610,6 +617,10 @@ int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word
     if (cudaStreamSynchronize(st) != cudaSuccess) return DSA_ERR_CUDA;
   }
   return DSA_OK;
+}
+
+uint64_t dsa_set_wait_limit(uint64_t cycles) {
+  return g_wait_cycles.exchange(cycles == 0 ? kWaitCycles : cycles);
 }
 
 int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream) {

@@ -92,7 +92,8 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_X + kXBufs * kXB;
   static constexpr int OFF_MASK = OFF_BAR + 512;  // [stage][4] slot-validity words
   static constexpr int OFF_MISC = OFF_MASK + 128;  // [0] TMEM base, [2] abort flag, [3] drain
-                                                  // flag, [6] the peer's abort flag (at exit)
+                                                  // flag, [6] the peer's abort flag (at exit),
+                                                  // [8] a split-K merge gave up waiting
   static constexpr int OFF_RED = OFF_MISC + 64;   // [2 hh][4 quadrants][kHT heads] floats
   static_assert(kTS % 16 == 0 && kTS <= 128 && kGroups <= 32 && kMaskWords <= 4, "tile shape");
   static constexpr int SMEM_USED = OFF_RED + 2 * 4 * kHT * 4;
@@ -237,6 +238,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     misc[2] = 0;
     misc[3] = 0;
     misc[6] = 0;
+    misc[8] = 0;
     ptx::fence_mbar_init();
     for (int b = 0; b < kXBufs; ++b) ptx::mbar_arrive_expect_tx(bar(B_XF + b), (uint32_t)kXB);
   }
@@ -264,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int64_t G = gridDim.x >> 1;
   const int64_t u_lo = u_begin(pair, p.units, G);
   const int64_t u_hi = u_begin(pair + 1, p.units, G);
-  const Waiter wait{misc + 2, p.err};
+  const Waiter wait{misc + 2, p.err, p.wait_cycles};
 
   if (warp == kQWarp) {
     // ------------------------------------------------------------------ Q loader
@@ -288,7 +290,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ++seg;
       }
       if (seg > 0) {
-        const Waiter drain{misc + 3, p.err};
+        const Waiter drain{misc + 3, p.err, p.wait_cycles};
         drain(bar(B_QF + ((seg - 1) % kQBufs)), (uint32_t)(((seg - 1) / kQBufs) & 1));
       }
     }
@@ -408,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
     if (!ok && lane == 0) {
-      const Waiter drain{misc + 3, p.err};
+      const Waiter drain{misc + 3, p.err, p.wait_cycles};
       for (int64_t li = n_issued - 1; li >= 0 && li >= n_issued - kStages; --li)
         drain(bar(B_KVF + (int)(li % kStages)), (uint32_t)((li / kStages) & 1));
     }
@@ -417,7 +419,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ score MMA issuer
     ptx::regs_dec<kRegsLow>();
     if (lane == 0) {
-      const Waiter wait{misc + 2, p.err, true};
+      const Waiter wait{misc + 2, p.err, p.wait_cycles, true};
       constexpr uint32_t kIdS = idesc_bf16(128, NH, false);
       // Descriptors of offset 0; an operand at byte offset o adds o >> 4.
       const uint64_t dk = desc(sbase + (uint32_t)OFF_KV, 16, 1024, kSw128);
@@ -464,7 +466,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ++seg;
       }
       if (!ok) {
-        const Waiter drain{misc + 3, p.err};
+        const Waiter drain{misc + 3, p.err, p.wait_cycles};
         ptx::umma_commit(bar(B_DRAIN));
         drain(bar(B_DRAIN), 0);
       }
@@ -477,7 +479,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // segment waits until the previous segment's epilogue has read O.
     ptx::regs_dec<kRegsLow>();
     if (lane == 0) {
-      const Waiter wait{misc + 2, p.err, true};
+      const Waiter wait{misc + 2, p.err, p.wait_cycles, true};
       constexpr uint32_t kIdPV = idesc_bf16(128, NH, true);
       const uint64_t dv = desc(sbase + (uint32_t)OFF_KV, kRB, 1024, kSw128);
       const uint64_t dp = desc(sbase + (uint32_t)OFF_P, 16, 1024, kSw128);
@@ -521,7 +523,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ++seg;
       }
       if (!ok) {
-        const Waiter drain{misc + 3, p.err};
+        const Waiter drain{misc + 3, p.err, p.wait_cycles};
         ptx::umma_commit(bar(B_DRAIN + 1));
         drain(bar(B_DRAIN + 1), 0);
       }
@@ -646,17 +648,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t want = (uint32_t)(p_hi - p_lo);
             const uint64_t t0 = ptx::cycles();
             uint32_t got = ptx::ld_acquire_gpu(cnt);
+            uint32_t lost = 0;
             while (got != want) {
-              if (ptx::cycles() - t0 > kWaitCycles || misc[2]) {
+              if (ptx::cycles() - t0 > p.wait_cycles || misc[2]) {
                 misc[2] = 1;
+                lost = 1;
                 atomicOr(p.err, (uint32_t)DSA_DEVERR_TIMEOUT);
                 break;
               }
               __nanosleep(32);
               got = ptx::ld_acquire_gpu(cnt);
             }
+            misc[8] = lost;
           }
           ptx::bar_sync(kNamedBar, kSmThreads);
+          // A merge that gave up would combine whatever partials are there: the row is
+          // written as NaN instead, next to the timeout bit in the error word.
+          const bool lost = misc[8] != 0u;
           float M[kHT], Lt[kHT], acc[2][kHT];
 #pragma unroll
           for (int h = 0; h < kHT; ++h) {
@@ -700,7 +708,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h = 0; h < kHT; ++h)
               p.out[b * p.out_sb + (int64_t)(h0 + kHT * hh + h) * p.out_sh + d] =
-                  __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
+                  lost ? __float2bfloat16_rn(NAN)
+                       : __float2bfloat16_rn(Lt[h] > 0.f ? acc[mt][h] / Lt[h] : 0.f);
           }
           if (rank == 0 && qd == 0 && lane < kHT) {
             float mh = 0.f, lh = 0.f;
@@ -711,7 +720,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 lh = Lt[h];
               }
             p.lse[b * p.lse_sb + (int64_t)(h0 + kHT * hh + lane) * p.lse_sh] =
-                lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY;
+                lost ? NAN : (lh > 0.f ? mh + ptx::lg2(lh) : -INFINITY);
           }
           // every part has been counted and read: the counter is ready for the next call
           if (warp == kSm0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;

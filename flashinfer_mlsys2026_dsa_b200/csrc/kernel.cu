@@ -70,14 +70,15 @@ void* workspace_for(int device, void* stream, size_t need) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(device);
-  if (w.ptr != nullptr) {
-    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
-    cudaFree(w.ptr);
-    w = Workspace{};
-  }
+  // The new buffer is allocated and cleared before the old one is released, so a failed
+  // allocation leaves the table entry as it was and raises on every call that needs more.
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, need);
   if (e == cudaSuccess) e = cudaMemset(p, 0, need);
+  if (e == cudaSuccess && w.ptr != nullptr) {
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream));  // calls in flight use the old one
+    cudaFree(w.ptr);
+  }
   cudaSetDevice(prev);
   if (e != cudaSuccess) {
     if (p != nullptr) cudaFree(p);

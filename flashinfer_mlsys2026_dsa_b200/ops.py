@@ -13,6 +13,7 @@ current CUDA stream.  There is no CPU path: CPU tensors raise.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 
 import torch
@@ -29,7 +30,32 @@ _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 class DSAError(RuntimeError):
-    """A non-zero status from the native library."""
+    """A non-zero status from the native library, or (strict mode) device error bits."""
+
+
+# Strict mode: every call synchronises its stream and raises DSAError when the kernel set
+# a device error bit (an out-of-range index treated as padding, or a wait that ran out, in
+# which case a split row was written as NaN).  Off by default, since the check costs a
+# stream synchronisation per call; DSA_STRICT=1 in the environment turns it on.
+_strict = os.environ.get("DSA_STRICT", "0") not in ("", "0")
+
+
+def set_strict(enabled: bool) -> bool:
+    """Turn strict mode on or off; returns the previous setting."""
+    global _strict
+    prev, _strict = _strict, bool(enabled)
+    return prev
+
+
+def _strict_check(device: torch.device, what: str) -> None:
+    word = read_device_errors(device, clear=True)
+    if word:
+        bits = []
+        if word & _native.DEVERR_BAD_INDEX:
+            bits.append("an index outside [-1, num_slots) was treated as padding")
+        if word & _native.DEVERR_TIMEOUT:
+            bits.append("a wait in the kernel ran out (rows whose split-K merge gave up are NaN)")
+        raise DSAError(f"{what}: device error word {word:#x}: " + "; ".join(bits))
 
 
 def _check(code: int, what: str) -> None:
@@ -101,12 +127,24 @@ def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
         raise ValueError(f"num_heads={H} is not supported (supported: {SUPPORTED_HEADS})")
 
 
-def _slot_view(cache: torch.Tensor, width: int) -> torch.Tensor:
-    """[..., page, width] cache as [num_slots, width] rows without copying when possible."""
+def _slot_view(cache: torch.Tensor, width: int, name: str) -> torch.Tensor:
+    """[..., page, width] cache as a [num_slots, width] slot table, always a view.
+
+    The pools are flattened the way fused.py:155-156 does (``reshape(-1, D)``), but a pool
+    that is not a uniform slot table (inner stride not 1, or pages not evenly spaced)
+    raises instead of being copied: a copy of a 1.5-20 GB pool per call would dwarf the
+    decode.
+    """
     if cache.stride(-1) != 1:
-        cache = cache.contiguous()
-    flat = cache.reshape(-1, width)  # a view for page-uniform strides (fused.py:155-156)
-    return flat
+        raise ValueError(f"{name} must have a unit inner stride (got strides {cache.stride()})")
+    try:
+        return cache.view(-1, width)
+    except RuntimeError:
+        pass
+    if cache.dim() == 3 and cache.stride(0) == cache.stride(1) * cache.shape[1]:
+        return cache.as_strided((cache.shape[0] * cache.shape[1], width), (cache.stride(1), 1))
+    raise ValueError(f"{name} is not a uniform slot table: pages of shape {tuple(cache.shape)} "
+                     f"with strides {cache.stride()} cannot be addressed with one slot stride")
 
 
 def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output, lse) -> None:
@@ -129,6 +167,8 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
             rc = ext.decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, float(sm_scale),
                             output, lse, ws, stream)
             if rc == _native.DSA_OK:
+                if _strict:
+                    _strict_check(q_nope.device, "dsa_sparse_mla_decode")
                 return
             if rc not in _REVALIDATE:
                 _check(rc, "dsa_sparse_mla_decode")
@@ -144,8 +184,8 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
         q_pe = q_pe.contiguous()
     if sparse_indices.stride(-1) != 1:
         sparse_indices = sparse_indices.contiguous()
-    ckv = _slot_view(ckv_cache, D_CKV)
-    kpe = _slot_view(kpe_cache, D_KPE)
+    ckv = _slot_view(ckv_cache, D_CKV, "ckv_cache")
+    kpe = _slot_view(kpe_cache, D_KPE, "kpe_cache")
     if ckv.shape[0] != kpe.shape[0]:
         raise ValueError("ckv_cache and kpe_cache hold different slot counts")
     out_t = output if output.stride(-1) == 1 else torch.empty_like(output, memory_format=torch.contiguous_format)
@@ -165,6 +205,8 @@ def kernel(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output,
     _check(rc, "dsa_sparse_mla_decode")
     if out_t is not output:
         output.copy_(out_t)
+    if _strict:
+        _strict_check(q_nope.device, "dsa_sparse_mla_decode")
 
 
 def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, page_table, positions, sm_scale, output,
@@ -209,8 +251,8 @@ def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, page_table, positions, sm_s
         positions = positions.contiguous()
     if page_table.stride(-1) != 1:
         page_table = page_table.contiguous()
-    ckv = _slot_view(ckv_cache, D_CKV)
-    kpe = _slot_view(kpe_cache, D_KPE)
+    ckv = _slot_view(ckv_cache, D_CKV, "ckv_cache")
+    kpe = _slot_view(kpe_cache, D_KPE, "kpe_cache")
     if ckv.shape[0] != kpe.shape[0]:
         raise ValueError("ckv_cache and kpe_cache hold different slot counts")
     out_t = output if output.stride(-1) == 1 else torch.empty_like(output, memory_format=torch.contiguous_format)
@@ -231,6 +273,8 @@ def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, page_table, positions, sm_s
     _check(rc, "dsa_sparse_mla_decode_paged")
     if out_t is not output:
         output.copy_(out_t)
+    if _strict:
+        _strict_check(q_nope.device, "dsa_sparse_mla_decode_paged")
 
 
 def decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):

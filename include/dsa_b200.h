@@ -46,7 +46,8 @@ enum {
 /* Bits of the sticky device error word kept in the workspace. */
 enum {
   DSA_DEVERR_BAD_INDEX = 1u, /* an index < -1 or >= num_slots was seen; treated as padding */
-  DSA_DEVERR_TIMEOUT = 2u    /* a pipeline wait ran past its bound; the CTA stopped early */
+  DSA_DEVERR_TIMEOUT = 2u    /* a wait ran past its bound; the CTA stopped early, and a
+                                split row whose merge gave up was written as NaN */
 };
 
 /*
@@ -132,6 +133,17 @@ size_t dsa_sparse_mla_decode_workspace_size(int64_t num_tokens, int32_t num_head
 int dsa_read_error_word(void* workspace, void* stream, int clear, uint32_t* word);
 
 /*
+ * Sets the bound of every wait inside the decode kernels (pipeline barriers and the
+ * split-K merge's wait for the other parts of a row) to `cycles` SM clock cycles for
+ * launches that follow; 0 restores the default of 4e9 cycles (about 2 s at the B200's
+ * ~2 GHz clock).  Returns the previous bound.  A wait that runs out sets
+ * DSA_DEVERR_TIMEOUT, and a split row whose merge gave up is written as NaN (output and
+ * lse).  Process-wide; a diagnostic for tests of the timeout path, which shorten the
+ * bound.  No counterpart in the reference (its kernels do not wait on one another).
+ */
+uint64_t dsa_set_wait_limit(uint64_t cycles);
+
+/*
  * Failure-detection self test: launches one CTA that waits on an mbarrier no
  * one arrives at, bounded by `timeout_ns` (counted as 2 SM clock cycles per ns,
  * i.e. about `timeout_ns` at the B200's ~2 GHz clock; the decode kernels bound
@@ -154,14 +166,19 @@ int dsa_selftest_bounded_wait(int64_t timeout_ns, void* workspace, void* stream)
  * every device that loads it, until the process exits; the call itself allocates
  * nothing (no cudaMalloc, cudaFree or allocating library routine).
  *   - The first call on a device resolves the array's device address (once per device,
- *     with that device current) and keeps it for later calls.
+ *     with that device current) and keeps it for later calls.  Do not use this entry
+ *     point across cudaDeviceReset() on that device: the module may be reloaded at
+ *     another address.
  *   - Limit: 8448 bytes of header and split-K counters, plus, when rows are split
  *     between cluster pairs of the persistent grid, one partial per pair (32,896 bytes
  *     for 16-head rows, 65,792 bytes for wider rows, which run as 32-head groups).  A
- *     call whose (row, head group) count fits the grid (at most 74 on a 148-SM B200,
- *     e.g. 64 rows of 16 or 32 heads) splits no row and always fits; a larger call runs
- *     split rows on every pair and needs 2.4 MB or more, beyond the array: it returns
- *     DSA_ERR_SCRATCH_LIMIT (use dsa_sparse_mla_decode).
+ *     call whose (row, head group) count is at most the number of two-CTA clusters the
+ *     device runs at once (its persistent grid: half the SM count on a B200, 74 pairs on
+ *     148 SMs, e.g. 74 rows of 16 heads or 64 rows of 32 heads) splits no row and always
+ *     fits; a larger call runs split rows on every pair and needs 2.4 MB or more, beyond
+ *     the array: it returns DSA_ERR_SCRATCH_LIMIT (use dsa_sparse_mla_decode).  The
+ *     split path of this entry point is therefore reachable only on devices with fewer
+ *     cluster pairs.
  *   - Every call on a device shares the array and finds the previous call's bytes there:
  *     the call clears the first 8448 bytes (error word and split-K arrival counters;
  *     device error bits are not reported by this entry point) and always writes the
