@@ -66,10 +66,11 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return d;
 }
 
-// Instruction descriptor, kind::f16: bf16 A/B, fp32 D.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major) {
+// Instruction descriptor, kind::f16: bf16 A/B, fp32 D; A and B K-major unless flagged.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
+                                                  bool b_mn_major = false) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Byte offset of element (row h, column k) in a [rows x 64] bf16 tile stored
@@ -154,7 +155,9 @@ __global__ void selftest_wait_kernel(uint32_t* err, int64_t timeout_ns) {
 
 }  // namespace dsa
 
+#include "dsa_pipeline.cuh"
 #include "dsa_decode_h16.cuh"
+#include "dsa_decode_hm.cuh"
 
 namespace dsa {
 // ====================================================================== host side
@@ -214,15 +217,18 @@ const KernelVariant kVariants[] = {
     {16, true, h16::dsa_decode_h16_kernel<16, true>, h16::Cfg<16>::SMEM_BYTES},
     {32, false, h16::dsa_decode_h16_kernel<32, false>, h16::Cfg<32>::SMEM_BYTES},
     {32, true, h16::dsa_decode_h16_kernel<32, true>, h16::Cfg<32>::SMEM_BYTES},
+    {128, false, hm::dsa_decode_hm_kernel<false>, hm::SMEM_BYTES},
+    {128, true, hm::dsa_decode_hm_kernel<true>, hm::SMEM_BYTES},
 };
 const KernelVariant& variant(int nh, bool paged) {
   for (const KernelVariant& kv : kVariants)
     if (kv.nh == nh && kv.paged == paged) return kv;
   return kVariants[0];
 }
-// Heads per work unit: 16 for 16-head rows, 32 otherwise (a 128-head row is 4 units).
-int group_heads(int num_heads) { return num_heads == 16 ? 16 : 32; }
-constexpr size_t kMaxSlotFloats = (size_t)h16::Cfg<32>::kSlotFloats;
+// Heads per work unit: 16 for 16-head rows, 32 for 32- and 64-head rows (two units per
+// 64-head row), 128 for 128-head rows (the heads-as-M kernel: one unit per row and tile).
+int group_heads(int num_heads) { return num_heads == 16 ? 16 : (num_heads == 128 ? 128 : 32); }
+constexpr size_t kMaxSlotFloats = (size_t)hm::kSlotFloats;
 
 // Sets the decode kernels' shared-memory attribute and returns how many of their clusters
 // fit on the device at once (the persistent grid's size), 0 on error.
@@ -266,8 +272,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 //   [0, 256)            header (word 0: sticky device error bits)
 //   [256, 8448)         split-K arrival counters, 2 per CTA pair (one per rank; each
 //                       returns to zero when its row is merged)
-//   [8448, ...)         split-K partials: one slot per SM (at most one is used per CTA
-//                       pair), each sized for a 32-head group (O, m and l: 65,792 bytes)
+//   [8448, ...)         split-K partials: one slot per CTA pair (two SMs), each sized for
+//                       a 128-head row (O, m and l: 263,168 bytes)
 constexpr size_t kCountersOff = 256;
 constexpr size_t kPartsOff = 8448;
 constexpr int kMaxPairs = (int)((kPartsOff - kCountersOff) / 8);
@@ -279,8 +285,8 @@ struct WsLayout {
 WsLayout ws_layout(int sms) {
   WsLayout w;
   w.parts_off = kPartsOff;
-  // one partial slot per cluster pair (at most one per two SMs; one per SM is room to spare)
-  w.total = align_up(w.parts_off + (size_t)sms * kMaxSlotFloats * 4, 256);
+  // one partial slot per cluster pair (a pair occupies two SMs)
+  w.total = align_up(w.parts_off + (size_t)((sms + 1) / 2) * kMaxSlotFloats * 4, 256);
   return w;
 }
 
@@ -430,10 +436,19 @@ int make_plan(const DecodeArgs& a, int dev, Plan& pl) {
   if (cap <= 0) return DSA_ERR_CUDA;
   pl.nh = group_heads(a.num_heads);
   const int hg = a.num_heads / pl.nh;  // head groups per row
-  const int ts = pl.nh == 16 ? h16::Cfg<16>::kTS : h16::Cfg<32>::kTS;  // slots per tile
+  const int ts = pl.nh == 16 ? h16::Cfg<16>::kTS
+                             : (pl.nh == 32 ? h16::Cfg<32>::kTS : hm::kTS);  // slots per tile
   pl.tpr = (a.topk + ts - 1) / ts;
   const int64_t num_rh = a.num_tokens * hg;
   pl.units = num_rh * (int64_t)pl.tpr;
+  if (pl.nh == 128) {
+    // 128-head rows: stream-K over all pairs whatever the row count (a 128-head row is a
+    // long unit, so its merge is cheap next to idle SMs); every pair may hold a partial.
+    pl.grid = (int)(pl.units < cap ? pl.units : cap);
+    if (pl.grid > kMaxPairs) pl.grid = kMaxPairs;
+    pl.need = kPartsOff + (size_t)pl.grid * (size_t)hm::kSlotFloats * 4;
+    return DSA_OK;
+  }
   // With no more (row, group) pairs than the grid holds, each gets a whole cluster pair and
   // none is split: a split-K merge costs a few dependent global round trips on the tail,
   // each slow while the other SMs saturate HBM, which outweighs the idle SMs.  Otherwise
@@ -516,9 +531,17 @@ int current_device(int& dev) {
   return DSA_OK;
 }
 
+// The 128-head kernel writes each head's output with 16-byte stores.
+int check_out_alignment(const DecodeArgs& a) {
+  if (a.num_heads == 128 && (!aligned16(a.out) || (a.out_sb * 2) % 16 || (a.out_sh * 2) % 16))
+    return DSA_ERR_MISALIGNED;
+  return DSA_OK;
+}
+
 int decode_with_workspace(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
                           void* stream) {
   int rc = check_args(a);
+  if (rc == DSA_OK && a.num_tokens > 0) rc = check_out_alignment(a);
   if (rc != DSA_OK || a.num_tokens == 0) return rc;
   int dev = 0;
   if ((rc = current_device(dev)) != DSA_OK) return rc;
@@ -660,6 +683,7 @@ extern "C" int dsa_sparse_mla_decode_noalloc(
                      output_stride_h, lse,             lse_stride_b,    lse_stride_h,
                      num_tokens,      num_heads,       topk};
   int rc = check_args(a);
+  if (rc == DSA_OK && num_tokens > 0) rc = check_out_alignment(a);
   if (rc != DSA_OK || num_tokens == 0) return rc;
   int dev = 0;
   if ((rc = current_device(dev)) != DSA_OK) return rc;

@@ -36,15 +36,15 @@
 namespace dsa {
 namespace h16 {
 
-constexpr int kBlk = 4;                  // 64-wide ckv d-blocks per CTA
+constexpr int kBlk = pipe::kBlk;         // 64-wide ckv d-blocks per CTA
 constexpr int kStages = 3;
 constexpr int kMaskStride = 8;           // mask words per stage: [0, 4) slot bits, [7] any
-constexpr int kMaskAny = 7;
+constexpr int kMaskAny = pipe::kMaskAny;
 constexpr int OFF_KV = 0;
 constexpr int kThreads = 512;
 constexpr int kQWarp = 0;
 constexpr int kProd0 = 1;
-constexpr int kProdWarps = kBlk + 1;
+constexpr int kProdWarps = pipe::kProdWarps;
 constexpr int kMmaWarp = 6;     // score issuer; also allocates TMEM
 constexpr int kPvWarp = 7;
 constexpr int kSm0 = 8;
@@ -56,7 +56,8 @@ constexpr uint32_t kNamedBar = 1;
 constexpr uint32_t kRegsLow = 72;
 constexpr uint32_t kRegsHigh = 184;
 static_assert(256 * (kRegsLow + kRegsHigh) <= 65536, "register split exceeds the pool");
-constexpr uint32_t kSw128 = 2, kSw64 = 4;  // UMMA descriptor layout types
+using pipe::kSw128;
+using pipe::kSw64;
 
 // What depends on the head-group width NH (the N of both MMAs): 16 for H = 16, 32 for
 // H = 32, 64, 128 (a 128-head row is then 4 units instead of 8, each tile doing twice the
@@ -127,7 +128,7 @@ enum : int {
   B_DRAIN = B_OF + 1,            // [2] used only when an issuer stops early
   B_COUNT = B_DRAIN + 2
 };
-__host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * 5 + blk; }
+__host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * kProdWarps + blk; }
 // The exchange buffers X need no "empty" barrier.  A thread sends its partial of tile j
 // (into the peer's X[j % 2]) only after it finished tile j - 1, whose X wait needed every
 // peer thread's partial of tile j - 1; a peer thread sends that only after it finished
@@ -136,52 +137,7 @@ __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage
 static_assert(B_COUNT * 8 <= 512, "barrier block");
 static_assert(kStages * kMaskStride * 4 <= 128, "mask words");
 
-__device__ __forceinline__ uint64_t desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
-                                         uint32_t layout) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) |
-         ((uint64_t)layout << 61);
-}
-
-// Index entries of tile t of (row, head group) rh for a producer lane's group g: slot
-// ids, or token positions in a paged call; -1 past topk.
-template <int kTS>
-__device__ __forceinline__ void tile_entries(const Params& p, int64_t rh, int t, bool has, int g,
-                                             int (&r)[4]) {
-  const int32_t* ir = p.idx + (rh >> p.hg_shift) * p.idx_sb;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int k = t * kTS + 4 * g + e;
-    r[e] = (has && k < p.topk) ? __ldg(ir + k) : -1;
-  }
-}
-
-// Slot ids of a paged call's token positions: slot = page_table[row][pos >> pg_shift] *
-// page_size + (pos & (page_size - 1)), the flat slot the pool's [pages, page_size, D] layout
-// gives (fused.py:155-156).  -1 stays padding; a position past the row's table, a negative
-// page or a slot beyond int32 becomes -2, which the producer flags as a bad index.
-__device__ __forceinline__ void translate(const Params& p, int64_t rh, const int (&pos)[4],
-                                          int (&r)[4]) {
-  const int32_t* pr = p.pt + (rh >> p.hg_shift) * p.pt_sb;
-  const int mask = (1 << p.pg_shift) - 1;
-  int page[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int q = pos[e];
-    const bool in_table = q >= 0 && (q >> p.pg_shift) < p.pt_cols;
-    page[e] = in_table ? __ldg(pr + (q >> p.pg_shift)) : (q == -1 ? -1 : -2);
-  }
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int q = pos[e];
-    if (q < 0 || page[e] < 0) {
-      r[e] = (q == -1) ? -1 : -2;
-    } else {
-      const int64_t slot = ((int64_t)page[e] << p.pg_shift) | (int64_t)(q & mask);
-      r[e] = slot > (int64_t)INT32_MAX ? -2 : (int)slot;
-    }
-  }
-}
+using pipe::desc;
 
 // kPaged: sparse_indices holds token positions, translated through the page table by the
 // gather producers (ids are fetched two tiles ahead so the dependent page-table load is off
@@ -200,7 +156,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int OFF_MASK = C::OFF_MASK, OFF_MISC = C::OFF_MISC, OFF_RED = C::OFF_RED;
   constexpr int TMEM_COLS = C::TMEM_COLS, S_COL = C::S_COL, O_COL = C::O_COL;
   constexpr int kSlotFloats = C::kSlotFloats;
-  constexpr int kTS = C::kTS, kRB = C::kRB, kStageB = C::kStageB, kGroups = C::kGroups;
+  constexpr int kTS = C::kTS, kRB = C::kRB, kStageB = C::kStageB;
   constexpr int kPVKs = C::kPVKs;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
@@ -271,149 +227,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == kQWarp) {
     // ------------------------------------------------------------------ Q loader
     ptx::regs_dec<kRegsLow>();
-    if (lane == 0) {
-      int seg = 0;
-      int64_t u = u_lo;
-      Segment s;
-      while (next_segment(u, u_hi, p.tpr, s)) {
-        const int qb = seg % kQBufs;
-        if (!wait(bar(B_QE + qb), (uint32_t)(((seg / kQBufs) & 1) ^ 1))) break;
-        ptx::mbar_arrive_expect_tx(bar(B_QF + qb), (uint32_t)kQB);
-        const uint32_t qd = sbase + (uint32_t)(OFF_Q + qb * kQB);
-        const int b = (int)(s.rh >> p.hg_shift);
-        const int h0 = NH * (int)(s.rh & ((1 << p.hg_shift) - 1));
-        for (int j = 0; j < kBlk; ++j)
-          ptx::tma_load_3d(qd + (uint32_t)(j * C::kQBlk), &tm_qn, (int)(256 * rank) + 64 * j, h0,
-                           b, bar(B_QF + qb));
-        ptx::tma_load_3d(qd + (uint32_t)(kBlk * C::kQBlk), &tm_qp, (int)(32 * rank), h0, b,
-                         bar(B_QF + qb));
-        ++seg;
-      }
-      if (seg > 0) {
-        const Waiter drain{misc + 3, p.err, p.wait_cycles};
-        drain(bar(B_QF + ((seg - 1) % kQBufs)), (uint32_t)(((seg - 1) / kQBufs) & 1));
-      }
-    }
+    if (lane == 0)
+      pipe::q_loader<NH>(p, &tm_qn, &tm_qp, rank, sbase + (uint32_t)OFF_Q, bar(B_QF), bar(B_QE),
+                         u_lo, u_hi, wait, misc + 3);
     __syncwarp();
   } else if (warp >= kProd0 && warp < kProd0 + kProdWarps) {
     // ------------------------------------------------------------------ gather producers
     ptx::regs_dec<kRegsLow>();
-    const int blk = warp - kProd0;  // 0..3: ckv d-block of this CTA's half; 4: kpe half
-    const int g = lane;
-    const bool has = g < kGroups;
-    const bool is_kpe = blk == kBlk;
-    const uint32_t dst_off =
-        is_kpe ? (uint32_t)(kBlk * kRB + g * 256) : (uint32_t)(blk * kRB + g * 512);
-    const int col = is_kpe ? (int)(32 * rank) : (int)(256 * rank) + 64 * blk;
-    const uint32_t req_bytes = is_kpe ? 256u : 512u;
-    const CUtensorMap* map = is_kpe ? &tm_kpe : &tm_ckv;
-    const uint64_t policy = ptx::policy_evict_first();
-    bool ok = true;
-    int64_t n_issued = 0;
-    int cur[4], nxt[4], ahead[4];
-    // (rh, t) of the tile whose entries are fetched next, stepped without divisions
-    int64_t n_rh = u_lo / p.tpr;
-    int n_t = (int)(u_lo - n_rh * p.tpr);
-    int64_t a_rh = n_rh;  // paged: row of the positions held in `ahead`
-    // paged: pull a row's page table into L2 when the producers reach the row (d-block 0's
-    // warp; 128-byte lines), so the translations read it from L2
-    auto pf_row = [&](int64_t rh) {
-      if constexpr (kPaged) {
-        if (blk != 0) return;
-        const int32_t* pr = p.pt + (rh >> p.hg_shift) * p.pt_sb;
-        for (int c = lane * 32; c < p.pt_cols; c += 32 * 32)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(pr + c));
-      }
-    };
-    if (u_lo < u_hi) pf_row(n_rh);
-    if (u_lo < u_hi) {
-      tile_entries<kTS>(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
-      if constexpr (kPaged) translate(p, n_rh, ahead, cur);
-    }
-    if constexpr (kPaged) {
-      if (++n_t == p.tpr) {
-        n_t = 0;
-        ++n_rh;
-      }
-      a_rh = n_rh;
-      if (u_lo + 1 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, ahead);
-    }
-    int st = 0;
-    uint32_t phase = 0;
-    for (int64_t uu = u_lo, i = 0; uu < u_hi; ++uu, ++i) {
-      if constexpr (kPaged) {
-        // slot ids of tile uu + 1 from the positions fetched one tile earlier, then the
-        // positions of tile uu + 2
-        if (uu + 1 < u_hi) translate(p, a_rh, ahead, nxt);
-      }
-      if (++n_t == p.tpr) {
-        n_t = 0;
-        ++n_rh;
-        if (uu + 2 < u_hi) pf_row(n_rh);
-      }
-      if constexpr (kPaged) {
-        a_rh = n_rh;
-        if (uu + 2 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, ahead);
-      } else {
-        if (uu + 1 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, nxt);
-      }
-      uint32_t nib = 0;
-      bool bad = false;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (cur[e] < -1 || (int64_t)cur[e] >= p.num_slots) {
-          bad = true;
-          cur[e] = -1;
-        }
-        nib |= (cur[e] >= 0 ? 1u : 0u) << e;
-      }
-      // In a tile with any valid slot every group is requested: a padding slot's id is
-      // out of range, so the copy fills its row with zeros, and PV reads 0 * 0 there
-      // instead of stale bytes.  An all-padding tile is not requested at all (its score
-      // and PV are skipped).  Every producer warp sees the same ids, so the same tiles.
-      const bool tile_live = __ballot_sync(0xffffffffu, nib != 0u) != 0u;
-      const bool issue = has && tile_live;
-      const uint32_t n_req = (uint32_t)__popc(__ballot_sync(0xffffffffu, issue));
-      uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
-      if (blk == 0) {
-        if (bad) atomicOr(p.err, (uint32_t)DSA_DEVERR_BAD_INDEX);
-        const uint32_t sh = nib << (4 * (g & 7));
-        w0 = __reduce_or_sync(0xffffffffu, (g >> 3) == 0 ? sh : 0u);
-        w1 = __reduce_or_sync(0xffffffffu, (g >> 3) == 1 ? sh : 0u);
-        w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
-        w3 = __reduce_or_sync(0xffffffffu, (g >> 3) == 3 ? sh : 0u);
-      }
-      if (lane == 0) {
-        ok = wait(bar(kve(st, blk)), phase ^ 1u);
-        if (ok) {
-          if (blk == 0) {
-            masks[st * kMaskStride + 0] = w0;
-            masks[st * kMaskStride + 1] = w1;
-            masks[st * kMaskStride + 2] = w2;
-            masks[st * kMaskStride + 3] = w3;
-            masks[st * kMaskStride + kMaskAny] = w0 | w1 | w2 | w3;  // nonzero: a valid slot
-          }
-          ptx::mbar_arrive_expect_tx(bar(B_KVF + st), n_req * req_bytes);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
-      if (!ok) break;
-      n_issued = i + 1;
-      if (issue)
-        ptx::tma_gather4(sbase + (uint32_t)(OFF_KV + st * kStageB) + dst_off, map, col,
-                         make_int4(cur[0], cur[1], cur[2], cur[3]), bar(B_KVF + st), policy);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) cur[e] = nxt[e];
-      if (++st == kStages) {
-        st = 0;
-        phase ^= 1u;
-      }
-    }
-    if (!ok && lane == 0) {
-      const Waiter drain{misc + 3, p.err, p.wait_cycles};
-      for (int64_t li = n_issued - 1; li >= 0 && li >= n_issued - kStages; --li)
-        drain(bar(B_KVF + (int)(li % kStages)), (uint32_t)((li / kStages) & 1));
-    }
+    pipe::gather_producer<kTS, kStageB, kStages, kMaskStride, kPaged>(
+        p, &tm_ckv, &tm_kpe, warp - kProd0, lane, rank, sbase + (uint32_t)OFF_KV, masks, bar(B_KVF),
+        bar(B_KVE), u_lo, u_hi, wait, misc + 3);
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ score MMA issuer

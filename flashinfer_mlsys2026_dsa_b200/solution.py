@@ -28,7 +28,9 @@ ENTRY_POINT = "kernel.cu::kernel"
 SOURCE_FILES = (
     ("kernel.cu", os.path.join(_build.CSRC, "kernel.cu")),
     ("dsa_decode.cu", os.path.join(_build.CSRC, "dsa_decode.cu")),
+    ("dsa_pipeline.cuh", os.path.join(_build.CSRC, "dsa_pipeline.cuh")),
     ("dsa_decode_h16.cuh", os.path.join(_build.CSRC, "dsa_decode_h16.cuh")),
+    ("dsa_decode_hm.cuh", os.path.join(_build.CSRC, "dsa_decode_hm.cuh")),
     ("sm100_ptx.cuh", os.path.join(_build.CSRC, "sm100_ptx.cuh")),
     ("dsa_b200.h", os.path.join(_build.INCLUDE, "dsa_b200.h")),
 )
