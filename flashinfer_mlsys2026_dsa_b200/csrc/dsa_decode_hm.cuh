@@ -80,6 +80,8 @@ enum : int {
   B_OF,                                   // the epilogue has read O
   B_PW,                                   // a split-K partial is written (8 warps)
   B_CNT,                                  // the merge's arrival count has been read
+  B_MRG,                                  // another part's partial is in shared memory
+  B_MRE,                                  // ... and has been added into O (4 warps)
   B_DRAIN,                                // [2] used only when an issuer stops early
   B_COUNT = B_DRAIN + 2
 };
@@ -139,6 +141,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::mbar_init(bar(B_OF), kSoftmaxWarps);
     ptx::mbar_init(bar(B_PW), kSoftmaxWarps);
     ptx::mbar_init(bar(B_CNT), 1);
+    ptx::mbar_init(bar(B_MRG), 1);
+    ptx::mbar_init(bar(B_MRE), kSoftmaxWarps);
     misc[2] = 0;
     misc[3] = 0;
     misc[6] = 0;
@@ -332,6 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int64_t i = 0;        // tiles done by this CTA
     int pw_phase = 0;     // B_PW phases used so far (partials written)
     int cnt_phase = 0;    // B_CNT phases used so far (merges)
+    int mrg_phase = 0;    // B_MRG / B_MRE phases used so far (parts merged)
     bool aborted = false;
     int64_t u = u_lo;
     Segment s;
@@ -434,7 +439,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // A merge that gave up would combine whatever partials are there: the row is written
         // as NaN instead, next to the timeout bit in the error word.
         const bool lost = !__all_sync(0xffffffffu, cnt_ok) || misc[8] != 0u;
-        // final max over the live parts, their weights, then O in chunks of 32 columns
+        // final max over the live parts and their weights (one pass over the scalars)
         float M = l > 0.f ? m : -INFINITY;
         for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
           const float* pp = p.parts + cc * kSlotFloats;
@@ -443,58 +448,67 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const bool any = M != -INFINITY;
         const float w_own = (any && l > 0.f) ? ptx::ex2(m - M) : 0.f;
         float Lt = w_own * l;
+        // O = w_own O, then + w_j O_j for every other part j: the part's slab of this CTA's
+        // 256 columns (128 KB, contiguous) is copied into the pipeline's shared memory, free
+        // now that this segment's last PV is done, and added into O in tensor memory.
+        const uint32_t slab = sbase + (uint32_t)OFF_KV;
+        static_assert(NH * 256 * 4 <= OFF_X, "a part's slab fits in the stages and Q buffer");
         for (int64_t cc = p_lo + 1; cc <= p_hi; ++cc) {
           const float* pp = p.parts + cc * kSlotFloats;
           const float pl = __ldcg(pp + NH * kDCkv + NH + h);
-          if (pl > 0.f) Lt += ptx::ex2(__ldcg(pp + NH * kDCkv + h) - M) * pl;
+          const float wj = pl > 0.f ? ptx::ex2(__ldcg(pp + NH * kDCkv + h) - M) : 0.f;
+          Lt += wj * (pl > 0.f ? pl : 0.f);
+          if (warp == kSm0 + 4 && lane == 0) {
+            if (mrg_phase > 0) wait(bar(B_MRE), (uint32_t)((mrg_phase - 1) & 1));
+            ptx::fence_proxy_async_global();
+            ptx::mbar_arrive_expect_tx(bar(B_MRG), (uint32_t)(NH * 256 * 4));
+            ptx::bulk_g2s(slab, pp + part_o(0, d_half), (uint32_t)(NH * 256 * 4), bar(B_MRG));
+          }
+          const bool got = __all_sync(0xffffffffu, wait(bar(B_MRG), (uint32_t)(mrg_phase & 1)));
+          ptx::tc_fence_after();
+#pragma unroll 1
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const uint32_t ta = tmem + lane_base + (uint32_t)(O_COL + 32 * c8);
+            uint32_t r[32];
+            ptx::tmem_ld32(ta, r);
+            ptx::tmem_wait_ld();
+            const float wo = cc == p_lo + 1 ? w_own : 1.f;  // the own part's weight, once
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 o4 = got ? *reinterpret_cast<const float4*>(
+                                          sgen + OFF_KV + 4 * part_o(h, 32 * c8 + 4 * v))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float a[4] = {o4.x, o4.y, o4.z, o4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float own = __uint_as_float(r[4 * v + e]);
+                const float base = wo > 0.f ? wo * own : 0.f;  // stale O when wo == 0
+                r[4 * v + e] = __float_as_uint(wj > 0.f ? base + wj * a[e] : base);
+              }
+            }
+            ptx::tmem_st32(ta, r);
+          }
+          ptx::tmem_wait_st();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar(B_MRE));
+          ++mrg_phase;
         }
         const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
-        // the other parts' weights (0 for a part that saw only padding: its O is not used)
-        constexpr int kMaxParts = 2;  // parts read per pass over the columns
-        float wpart[kMaxParts];
+        ptx::tc_fence_after();
 #pragma unroll 1
         for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t r[32];
           ptx::tmem_ld32(tmem + lane_base + (uint32_t)(O_COL + 32 * c8), r);
           ptx::tmem_wait_ld();
           const int d0 = d_half + 32 * c8;
-          float acc[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) acc[c] = w_own > 0.f ? w_own * __uint_as_float(r[c]) : 0.f;
-          for (int64_t c0 = p_lo + 1; c0 <= p_hi; c0 += kMaxParts) {
-            // the loads of up to kMaxParts parts first, so that they cost one L2 round trip
-            float4 o4[kMaxParts][8];
-#pragma unroll
-            for (int j = 0; j < kMaxParts; ++j) {
-              const int64_t cc = c0 + j;
-              wpart[j] = 0.f;
-              if (cc > p_hi) continue;
-              const float* pp = p.parts + cc * kSlotFloats;
-              const float pl = __ldcg(pp + NH * kDCkv + NH + h);
-              if (pl > 0.f) wpart[j] = ptx::ex2(__ldcg(pp + NH * kDCkv + h) - M);
-#pragma unroll
-              for (int v = 0; v < 8; ++v)
-                o4[j][v] = __ldcg(reinterpret_cast<const float4*>(pp + part_o(h, d0 + 4 * v)));
-            }
-#pragma unroll
-            for (int j = 0; j < kMaxParts; ++j) {
-              if (!(wpart[j] > 0.f)) continue;
-#pragma unroll
-              for (int v = 0; v < 8; ++v) {
-                acc[4 * v] += wpart[j] * o4[j][v].x;
-                acc[4 * v + 1] += wpart[j] * o4[j][v].y;
-                acc[4 * v + 2] += wpart[j] * o4[j][v].z;
-                acc[4 * v + 3] += wpart[j] * o4[j][v].w;
-              }
-            }
-          }
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             uint4 wv;
-            wv.x = lost ? 0x7FC07FC0u : pack_bf16x2(acc[8 * v] * inv, acc[8 * v + 1] * inv);
-            wv.y = lost ? 0x7FC07FC0u : pack_bf16x2(acc[8 * v + 2] * inv, acc[8 * v + 3] * inv);
-            wv.z = lost ? 0x7FC07FC0u : pack_bf16x2(acc[8 * v + 4] * inv, acc[8 * v + 5] * inv);
-            wv.w = lost ? 0x7FC07FC0u : pack_bf16x2(acc[8 * v + 6] * inv, acc[8 * v + 7] * inv);
+            wv.x = lost ? 0x7FC07FC0u : pack_bf16x2(__uint_as_float(r[8 * v]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+            wv.y = lost ? 0x7FC07FC0u : pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+            wv.z = lost ? 0x7FC07FC0u : pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+            wv.w = lost ? 0x7FC07FC0u : pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + d0 + 8 * v) = wv;
           }
         }
@@ -549,13 +563,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mt = fmaxf(mt, x[k]);
           }
         }
-        // X is read: re-arm our barrier for the next tile (before this warp's release below,
-        // so that no byte of the next tile can arrive before the arming), then release the
-        // buffer to the peer's senders.
-        __syncwarp();
+        // X is read (every lane's loads have returned: the vote consumes their maximum):
+        // re-arm our barrier for the next tile (before this warp's release below, so that no
+        // byte of the next tile can arrive before the arming), then release the buffer to the
+        // peer's senders.
+        const uint32_t read_all = __ballot_sync(0xffffffffu, mt == mt);
         if (lane == 0) {
           if (warp == kSm0 + 4) ptx::mbar_arrive_expect_tx(bar(B_XF), (uint32_t)kXB);
-          ptx::mbar_arrive_remote(xe_peer);
+          ptx::mbar_arrive_remote_after(xe_peer, read_all == 0xFFFFFFFFu ? 0u : read_all);
         }
         // lazy rescale: only when the tile's max exceeds the running max by more than kTau
         float alpha = 1.f;

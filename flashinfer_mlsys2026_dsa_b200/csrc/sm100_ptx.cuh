@@ -91,6 +91,20 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* m, 
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// Contiguous global -> shared copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) that signals complete_tx on `bar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// Global data written through the generic proxy (and acquired) becomes visible to this
+// thread's later async-proxy reads of global memory (bulk copies) after this fence.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -253,11 +267,19 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t a, ui
       "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
       : "memory");
 }
-// Arrive once on an mbarrier of another CTA of the cluster (a shared::cluster address from
-// mapa); this thread's earlier memory accesses are ordered before the arrive.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
-               : "memory");
+// Relaxed arrive on an mbarrier of another CTA of the cluster (a shared::cluster address
+// from mapa).  The instruction takes `dep` as an operand and so issues only once `dep` has
+// been computed: a caller that must finish reading shared memory before the other CTA may
+// overwrite it passes a value computed from everything it read (the loads have then
+// returned).  A release-ordered arrive gives the same guarantee through the memory model
+// but waits for all of the thread's earlier memory operations at cluster scope, which
+// costs thousands of cycles here.  `dep` == 0xFFFFFFFF skips the arrive (never used).
+__device__ __forceinline__ void mbar_arrive_remote_after(uint32_t remote_bar, uint32_t dep) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0xFFFFFFFF;\n\t"
+      "@p mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];\n\t}" ::"r"(remote_bar),
+      "r"(dep)
+      : "memory");
 }
 // Every thread of every CTA of the cluster.
 __device__ __forceinline__ void cluster_sync() {
