@@ -620,6 +620,7 @@ def run_ours(args):
 
 
 def main():
+    global N_SETS
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -634,9 +635,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the other configurations and the 2048-row batch")
+    ap.add_argument("--sets", type=int, default=N_SETS,
+                    help="rotating input sets of the main workload (fewer keep an ncu capture "
+                         "small; the bytes of one set must still exceed the L2 for DRAM figures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    N_SETS = max(1, args.sets)
     if args.cpu_rows <= 0:
         from flashinfer_mlsys2026_dsa_b200.workloads import CONFIGS
         args.cpu_rows = max(1, min(CONFIGS[args.workload]["B"], os.cpu_count() or 1))
