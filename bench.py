@@ -23,6 +23,8 @@ Reported numbers:
              match the capture's digest.
   workloads  (one GPU) the other single-GPU configurations: b32_h128 (128 heads, with its
              tensor-pipe rate) and ragged_b256 (-1 padding), timed like `value`.
+  index_production  the step before the decode (each row's top-2048 positions of index
+             scores, as slot ids) alone and chained with the decode.
   b2048      (every N) the batch-sharded decode of a global batch of 2048 rows: each rank
              decodes its 2048/N rows against its own page pool, at most 1024 rows per
              call (a rank with more runs its rows as consecutive calls); per-GPU and
@@ -63,16 +65,19 @@ def _peaks():
         return {"hbm": 6650.0, "bf16": 1590.0, "source": "fallback"}
 
 
+DECODE_SOURCES = ("dsa_decode.cu", "dsa_decode_h16.cuh", "dsa_decode_hm.cuh", "dsa_pipeline.cuh",
+                  "sm100_ptx.cuh")
+
+
 def kernel_digest() -> str:
-    """SHA-256 (16 hex digits) of the CUDA sources the decode kernel is built from."""
+    """SHA-256 (16 hex digits) of the CUDA sources the decode kernels are built from."""
     import hashlib
 
     csrc = os.path.join(ROOT, "flashinfer_mlsys2026_dsa_b200", "csrc")
     h = hashlib.sha256()
-    for name in sorted(os.listdir(csrc)):
-        if name.endswith((".cu", ".cuh")) and name != "kernel.cu":
-            with open(os.path.join(csrc, name), "rb") as f:
-                h.update(name.encode() + b"\0" + f.read())
+    for name in DECODE_SOURCES:
+        with open(os.path.join(csrc, name), "rb") as f:
+            h.update(name.encode() + b"\0" + f.read())
     return h.hexdigest()[:16]
 
 
@@ -380,7 +385,8 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from flashinfer_mlsys2026_dsa_b200 import kernel, kernel_paged, read_device_errors, workloads
+    from flashinfer_mlsys2026_dsa_b200 import (kernel, kernel_paged, read_device_errors,
+                                               topk_slots, workloads)
 
     world, rank, local = _dist_setup(args.gpus)
     torch.cuda.set_device(local)
@@ -450,6 +456,42 @@ def run_ours(args):
                         max(1, math.ceil(args.warmup / N_SETS)), stream, barrier) * N_SETS * reps
     with torch.cuda.stream(stream):
         err |= read_device_errors(dev)
+
+    # ---------------- index production, the step before the decode: each row's top-k
+    # positions of index scores over its whole sequence, as slot ids, alone and chained
+    # with the decode (the ids cross HBM once, 8 KB per row)
+    index_rec = None
+    if not args.no_extra:
+        gsc = torch.Generator(device=dev).manual_seed(args.seed + 5)
+        topk_in = []
+        for w in sets:
+            sc = torch.randn(B, int(max(w.seq_lens)), generator=gsc, device=dev)
+            ln = torch.tensor(w.seq_lens, dtype=torch.int32, device=dev)
+            ids = torch.empty(B, w.topk, dtype=torch.int32, device=dev)
+            topk_in.append((sc, ln, ids, w))
+
+        def chained(a):
+            topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
+            kernel(a[3].q_nope, a[3].q_pe, a[3].ckv_cache, a[3].kpe_cache, a[2], a[3].sm_scale,
+                   out, lse)
+
+        warm = max(1, math.ceil(args.warmup / N_SETS))
+        t_ms = graph_ms([lambda a=a: topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
+                         for a in topk_in], reps, warm, stream, barrier)
+        c_ms = graph_ms([lambda a=a: chained(a) for a in topk_in], reps, warm, stream, barrier)
+        t_ms, c_ms = max_over_ranks([t_ms, c_ms], world, dev)
+        n_scores = sum(sum(a[3].seq_lens) for a in topk_in) / N_SETS
+        index_rec = {"topk_us_per_call": round(t_ms * 1e3, 2),
+                     "topk_then_decode_us_per_call": round(c_ms * 1e3, 2),
+                     "scores_per_call": int(n_scores),
+                     "scores_per_s": round(n_scores / (t_ms * 1e-3), 1),
+                     "method": "topk_slots(): fp32 index scores of every position of each row "
+                               "(seq_len 4k-32k) -> the 2048 best as slot ids, exact, one "
+                               "launch; then kernel() on those ids; CUDA-graph replay over "
+                               "the same 4 input sets as value"}
+        with torch.cuda.stream(stream):
+            err |= read_device_errors(dev)
+        del topk_in
 
     # ---------------- end to end through the public API, host buffers
     # Every step copies its query and index rows from pinned host memory, runs the public
@@ -610,6 +652,8 @@ def run_ours(args):
         "clocks": clk.summary(),
         "device_errors": err,
     }
+    if index_rec is not None:
+        line["index_production"] = index_rec
     if extra:
         line["workloads"] = extra
     if b2048 is not None:

@@ -6,8 +6,8 @@ Drop-in for the reference solution's entry point
 hand-written sm_100a CUDA kernel reached through the C ABI in include/dsa_b200.h.
 """
 from .ops import (DSAError, decode, kernel, kernel_paged, read_device_errors,  # noqa: F401
-                  set_strict, workspace_for)
+                  set_strict, topk_slots, workspace_for)
 
-__all__ = ["kernel", "kernel_paged", "decode", "read_device_errors", "set_strict",
-           "workspace_for", "DSAError"]
+__all__ = ["kernel", "kernel_paged", "decode", "topk_slots", "read_device_errors",
+           "set_strict", "workspace_for", "DSAError"]
 __version__ = "0.1.0"

@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = (
     "dsa_sparse_mla_decode",
     "dsa_sparse_mla_decode_paged",
     "dsa_sparse_mla_decode_noalloc",
+    "dsa_topk_slots",
     "dsa_sparse_mla_decode_workspace_size",
     "dsa_read_error_word",
     "dsa_selftest_bounded_wait",
@@ -83,6 +84,11 @@ def load(build_if_missing: bool = True):
         lib.dsa_sparse_mla_decode_paged.argtypes = _PAGED_ARGTYPES
         lib.dsa_sparse_mla_decode_noalloc.restype = _c.c_int
         lib.dsa_sparse_mla_decode_noalloc.argtypes = _DECODE_ARGTYPES[:-3] + [_c.c_void_p]
+        lib.dsa_topk_slots.restype = _c.c_int
+        lib.dsa_topk_slots.argtypes = [_c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p,
+                                       _c.c_int64, _c.c_int32, _c.c_int32, _c.c_int64,
+                                       _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_int64,
+                                       _c.c_void_p]
         lib.dsa_sparse_mla_decode_workspace_size.restype = _c.c_size_t
         lib.dsa_sparse_mla_decode_workspace_size.argtypes = [_c.c_int64, _c.c_int32, _c.c_int32,
                                                              _c.c_int32]

@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 INCLUDE = os.path.join(REPO_DIR, "include")
 LIB_NAME = "libdsa_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
-SOURCES = [os.path.join(CSRC, "dsa_decode.cu")]
+SOURCES = [os.path.join(CSRC, "dsa_decode.cu"), os.path.join(CSRC, "dsa_topk.cu")]
 TVM_BINDING = os.path.join(CSRC, "kernel.cu")
 # every source and header the library is built from (a change to any makes it stale)
 DEPS = sorted(

@@ -277,6 +277,54 @@ def kernel_paged(q_nope, q_pe, ckv_cache, kpe_cache, page_table, positions, sm_s
         _strict_check(q_nope.device, "dsa_sparse_mla_decode_paged")
 
 
+def topk_slots(scores, lengths, page_table, k, page_size=PAGE_SIZE, out=None):
+    """Index production: the decode's ``sparse_indices`` from index scores.
+
+    ``scores`` [rows, max_len] float32 CUDA tensor of the rows' token positions, ``lengths``
+    [rows] int32 (row b chooses among positions ``[0, lengths[b])``), ``page_table``
+    [rows, max_pages] int32 (the row's pool pages in order).  Returns (or writes into
+    ``out``) [rows, k] int32 slot ids ``page_table[b, pos // page_size] * page_size +
+    pos % page_size`` of each row's k highest-scoring positions, in ascending position
+    order, -1 after a row's positions when it has fewer than k (the decode's padding);
+    ties at the k-th score go to the smaller positions.  One launch on the current stream;
+    the result feeds :func:`kernel` directly.  The reference forms these ids on the caller
+    side (solution/triton/baseline.py:17-23); flashinfer names the step
+    ``top_k_page_table_transform``.
+    """
+    for name, t in (("scores", scores), ("lengths", lengths), ("page_table", page_table)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+    if scores.dtype != torch.float32:
+        raise TypeError(f"scores must be float32, got {scores.dtype}")
+    if lengths.dtype != torch.int32 or page_table.dtype != torch.int32:
+        raise TypeError("lengths and page_table must be int32")
+    if scores.dim() != 2 or page_table.dim() != 2:
+        raise ValueError("scores and page_table must be 2-D")
+    rows, max_len = scores.shape
+    if lengths.shape != (rows,) or page_table.shape[0] != rows:
+        raise ValueError("lengths must be [rows] and page_table [rows, max_pages]")
+    k = int(k)
+    page_size = int(page_size)
+    if k < 1 or page_size < 1 or page_size & (page_size - 1):
+        raise ValueError("k must be >= 1 and page_size a power of two")
+    if scores.stride(-1) != 1:
+        scores = scores.contiguous()
+    if page_table.stride(-1) != 1:
+        page_table = page_table.contiguous()
+    lengths = lengths.contiguous()
+    if out is None:
+        out = torch.empty(rows, k, dtype=torch.int32, device=scores.device)
+    elif out.shape != (rows, k) or out.dtype != torch.int32 or out.stride(-1) != 1:
+        raise ValueError(f"out must be an int32 [{rows}, {k}] tensor with a unit inner stride")
+    stream = torch._C._cuda_getCurrentRawStream(scores.get_device())
+    lib = _native._lib or _native.load()
+    _check(lib.dsa_topk_slots(scores.data_ptr(), scores.stride(0), lengths.data_ptr(),
+                              page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+                              page_size, rows, max_len, k, out.data_ptr(), out.stride(0), stream),
+           "dsa_topk_slots")
+    return out
+
+
 def decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):
     """Value-returning form of :func:`kernel`: returns (output, lse)."""
     B, H, _ = q_nope.shape

@@ -114,6 +114,32 @@ int dsa_sparse_mla_decode_paged(
     size_t workspace_bytes, void* stream);
 
 /*
+ * Index production: per-row top-k of index scores, written as the slot ids the decode takes.
+ * Replaces the caller-side step that builds `sparse_indices` for the reference's entry
+ * point (fused.py:150; its callers pass slot = page * 64 + offset of the selected token
+ * positions, baseline.py:17-23); the reference has no such kernel, and the published
+ * definition of the step is flashinfer's top_k_page_table_transform (top k of
+ * input[i, :lengths[i]], translated through the row's page table).
+ *
+ *   scores     [num_rows, >= max_len] fp32, row stride scores_stride_b: index scores of
+ *              the row's token positions
+ *   lengths    [num_rows] int32: row b selects among positions [0, min(lengths[b], max_len))
+ *   page_table [num_rows, >= page_table_cols] int32 as for dsa_sparse_mla_decode_paged
+ *   slots      [num_rows, >= k] int32 (written), row stride slots_stride_b
+ *
+ * Row b gets the slots of its k largest scores (ties at the k-th largest go to the smaller
+ * positions; scores are ordered by their IEEE-754 bit pattern: -0.0 below +0.0, NaN below
+ * every number), in ascending position order, then -1 up to k when the row has fewer than
+ * k positions.  A position past the row's table or on a negative page gives -1.  The
+ * result is exact and deterministic.  One launch on `stream`; nothing is allocated.
+ */
+int dsa_topk_slots(const float* scores, int64_t scores_stride_b, const int32_t* lengths,
+                   const int32_t* page_table, int64_t page_table_stride_b,
+                   int32_t page_table_cols, int32_t page_size, int64_t num_rows,
+                   int32_t max_len, int32_t k, int32_t* slots, int64_t slots_stride_b,
+                   void* stream);
+
+/*
  * Bytes of workspace dsa_sparse_mla_decode() needs for this problem on
  * `device` (split-K partials and the error word; the size depends only on
  * the device's SM count, so one workspace serves every shape).

@@ -156,3 +156,78 @@ int dsa_oracle_max_threads(void) {
   return 1;
 #endif
 }
+
+/* ---------------------------------------------------------------- index production
+ * Per-row top-k of index scores, translated to slot ids (the step that builds the decode's
+ * sparse_indices: slot = page_table[row][pos / page_size] * page_size + pos % page_size, as
+ * the reference's callers form page * 64 + offset, baseline.py:17-23; flashinfer publishes
+ * the step as top_k_page_table_transform: top k of input[i, :lengths[i]] through the row's
+ * table).  Selection: the k largest scores of scores[row, 0:L), L = clamp(lengths[row], 0,
+ * max_len), ordered by the IEEE-754 bit pattern (a larger float first, -0.0 below +0.0, NaN
+ * below every number), equal scores by the smaller position; the selected positions are
+ * written in ascending order, translated, then -1 up to k.  A position past the table or
+ * on a negative page gives -1.  Plain sort per row: test sizes only. */
+static inline uint32_t score_key(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return 0u; /* NaN */
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+typedef struct {
+  uint32_t key;
+  int32_t pos;
+} KeyPos;
+
+static int by_key_desc_pos_asc(const void* a, const void* b) {
+  const KeyPos* x = (const KeyPos*)a;
+  const KeyPos* y = (const KeyPos*)b;
+  if (x->key != y->key) return x->key > y->key ? -1 : 1;
+  return x->pos < y->pos ? -1 : (x->pos > y->pos ? 1 : 0);
+}
+
+static int by_int_asc(const void* a, const void* b) {
+  const int32_t x = *(const int32_t*)a, y = *(const int32_t*)b;
+  return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+int dsa_oracle_topk_slots(const float* scores, int64_t scores_sb, const int32_t* lengths,
+                          const int32_t* page_table, int64_t pt_sb, int32_t pt_cols,
+                          int32_t page_size, int64_t rows, int32_t max_len, int32_t k,
+                          int32_t* out, int64_t out_sb) {
+  KeyPos* kp = (KeyPos*)malloc(sizeof(KeyPos) * (size_t)(max_len > 0 ? max_len : 1));
+  int32_t* sel = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k > 0 ? k : 1));
+  if (!kp || !sel) return -1;
+  for (int64_t r = 0; r < rows; ++r) {
+    int32_t L = lengths[r];
+    if (L < 0) L = 0;
+    if (L > max_len) L = max_len;
+    const int32_t n = L < k ? L : k;
+    if (L <= k) {
+      for (int32_t i = 0; i < n; ++i) sel[i] = i;
+    } else {
+      for (int32_t i = 0; i < L; ++i) {
+        kp[i].key = score_key(scores[r * scores_sb + i]);
+        kp[i].pos = i;
+      }
+      qsort(kp, (size_t)L, sizeof(KeyPos), by_key_desc_pos_asc);
+      for (int32_t i = 0; i < k; ++i) sel[i] = kp[i].pos;
+      qsort(sel, (size_t)k, sizeof(int32_t), by_int_asc);
+    }
+    for (int32_t i = 0; i < k; ++i) {
+      int32_t s = -1;
+      if (i < n) {
+        const int32_t pos = sel[i], pg = pos / page_size;
+        if (pg < pt_cols) {
+          const int64_t page = page_table[r * pt_sb + pg];
+          const int64_t slot = page * page_size + pos % page_size;
+          if (page >= 0 && slot <= 2147483647LL) s = (int32_t)slot;
+        }
+      }
+      out[r * out_sb + i] = s;
+    }
+  }
+  free(kp);
+  free(sel);
+  return 0;
+}

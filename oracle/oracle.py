@@ -60,6 +60,11 @@ def _load():
                 ctypes.c_int32, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
                 ctypes.c_int32]
             lib.dsa_oracle_max_threads.restype = ctypes.c_int
+            lib.dsa_oracle_topk_slots.restype = ctypes.c_int
+            lib.dsa_oracle_topk_slots.argtypes = [
+                ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                ctypes.c_void_p, ctypes.c_int64]
             _lib = lib
     return _lib
 
@@ -178,3 +183,48 @@ def compact_pool(ckv_rows_fn, kpe_rows_fn, sparse_indices: np.ndarray):
     remap = np.searchsorted(slots, np.clip(safe, 0, None)).astype(np.int32)
     remap = np.where(safe == -1, -1, remap).astype(np.int32)
     return ckv_rows_fn(slots), kpe_rows_fn(slots), remap
+
+
+def topk_slots(scores, lengths, page_table, k: int, page_size: int):
+    """Index production in C: per-row top-k of ``scores`` [rows, max_len] (float32) over
+    the first ``lengths[row]`` entries, ties to the smaller position, selected positions in
+    ascending order translated through ``page_table`` [rows, cols] (int32), -1 up to k.
+    See ``dsa_oracle_topk_slots`` in dsa_oracle.c for the order of scores."""
+    lib = _load()
+    sc = np.ascontiguousarray(scores, dtype=np.float32)
+    ln = np.ascontiguousarray(lengths, dtype=np.int32)
+    pt = np.ascontiguousarray(page_table, dtype=np.int32)
+    rows, max_len = sc.shape
+    out = np.empty((rows, k), dtype=np.int32)
+    rc = lib.dsa_oracle_topk_slots(sc.ctypes.data, max_len, ln.ctypes.data, pt.ctypes.data,
+                                   pt.shape[1], pt.shape[1], int(page_size), rows, max_len,
+                                   int(k), out.ctypes.data, k)
+    if rc != 0:
+        raise MemoryError("oracle top-k: allocation failed")
+    return out
+
+
+def score_keys(scores) -> np.ndarray:
+    """Order-preserving uint32 keys of float32 scores (NaN lowest, -0.0 below +0.0)."""
+    u = np.ascontiguousarray(scores, dtype=np.float32).view(np.uint32)
+    nan = ((u & 0x7F800000) == 0x7F800000) & ((u & 0x007FFFFF) != 0)
+    key = np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint32)
+    return np.where(nan, np.uint32(0), key)
+
+
+def topk_slots_numpy(scores, lengths, page_table, k: int, page_size: int):
+    """Independent numpy restatement of :func:`topk_slots` (stable sort per row)."""
+    sc = np.asarray(scores, dtype=np.float32)
+    rows, max_len = sc.shape
+    out = np.full((rows, k), -1, dtype=np.int32)
+    for r in range(rows):
+        L = int(min(max(int(lengths[r]), 0), max_len))
+        if L <= k:
+            pos = np.arange(L)
+        else:
+            keys = score_keys(sc[r, :L]).astype(np.int64)
+            order = np.argsort(-keys, kind="stable")      # larger key first, ties by position
+            pos = np.sort(order[:k])
+        out[r, :len(pos)] = slots_from_positions(page_table[r:r + 1], pos[None, :].astype(np.int64),
+                                                 page_size)[0].clip(min=-1)
+    return out
