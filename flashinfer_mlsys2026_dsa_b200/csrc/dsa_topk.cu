@@ -11,10 +11,11 @@
 // result is one deterministic array.
 //
 // One CTA per row (1024 threads).  Scores are mapped to order-preserving 32-bit keys; a
-// radix select finds the k-th largest key T in three histogram passes over 12, 12 and 8 key
-// bits (each later pass only over the keys that share the bits already fixed); a counting
-// pass and an ordered compaction pass then write every position with key > T and the
-// first ones with key == T.  Each warp owns one contiguous segment of the row and reads it
+// radix select finds the k-th largest key T in four histogram passes over the key's bytes,
+// high to low (each later pass only over the keys that share the bytes already fixed), with
+// one 256-bin histogram per warp so that warps never contend for a counter; a counting pass
+// and an ordered compaction pass then write every position with key > T and the first
+// ones with key == T.  Each warp owns one contiguous segment of the row and reads it
 // coalesced, so positions come out in order without a sort.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -26,7 +27,7 @@ namespace topk {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 4096;
+constexpr int kBins = 256;  // one key byte per pass
 
 struct Params {
   const float* scores;
@@ -83,35 +84,26 @@ __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, uint32_t* w
   return r;
 }
 
-// Given the histogram `hist[nbins]` of the candidate keys and `need` (>= 1) elements still to
-// take from the top, the bin holding the need-th largest candidate and how many of the
-// candidates in higher bins are taken (through *above).  Thread t owns bins
-// [nbins - (t + 1) * per, nbins - t * per), scanned from the top.
-__device__ __forceinline__ int select_bin(const uint32_t* hist, int nbins, uint32_t need,
-                                          uint32_t* wsum, uint32_t* above, int* bin_out) {
-  const int per = nbins / kThreads > 0 ? nbins / kThreads : 1;
-  const int hi = nbins - threadIdx.x * per;  // exclusive
-  uint32_t mine = 0;
-  if (hi > 0)
-    for (int b = hi - 1; b >= hi - per && b >= 0; --b) mine += hist[b];
-  const uint32_t incl = block_inclusive_scan(mine, wsum);  // count in bins >= hi - per
-  const uint32_t excl = incl - mine;                       // count in bins >= hi
-  if (hi > 0 && excl < need && incl >= need) {
-    uint32_t acc = excl;
-    for (int b = hi - 1; b >= hi - per; --b) {
-      if (acc + hist[b] >= need) {
-        *bin_out = b;
-        *above = acc;
-        break;
-      }
-      acc += hist[b];
-    }
+// Given the histogram `hist[kBins]` of the candidate keys' current byte and `need` (>= 1)
+// elements still to take from the top, the bin holding the need-th largest candidate, and
+// through *above how many candidates lie in higher bins.  Thread t < kBins owns bin
+// kBins - 1 - t (so the scan runs from the top bin down).
+__device__ __forceinline__ int select_bin(const uint32_t* hist, uint32_t need, uint32_t* wsum,
+                                          uint32_t* above, int* bin_out) {
+  const int b = kBins - 1 - (int)threadIdx.x;
+  const uint32_t mine = b >= 0 ? hist[b] : 0u;
+  const uint32_t incl = block_inclusive_scan(mine, wsum);  // candidates in bins >= b
+  const uint32_t excl = incl - mine;                       // candidates in bins > b
+  if (b >= 0 && excl < need && incl >= need) {
+    *bin_out = b;
+    *above = excl;
   }
   __syncthreads();
   return *bin_out;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p) {
+  __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t wsum[32];
   __shared__ uint32_t above_s;
@@ -131,39 +123,33 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     return;
   }
 
-  // ---- radix select of the k-th largest key: bits [31:20], [19:8], [7:0]
+  // ---- radix select of the k-th largest key, one key byte per pass (bits 31..24 first)
   uint32_t prefix = 0, need = (uint32_t)k;
-  const int shifts[3] = {20, 8, 0};
-  const int nbins[3] = {4096, 4096, 256};
-  for (int pass = 0; pass < 3; ++pass) {
-    for (int b = threadIdx.x; b < kBins; b += kThreads) hist[b] = 0u;
-    __syncthreads();
-    const int sh = shifts[pass];
-    const uint32_t bmask = (uint32_t)nbins[pass] - 1u;
-    const int hsh = sh + (pass == 0 ? 12 : (pass == 1 ? 12 : 8));  // bits above this digit
-    // every lane of a warp runs every iteration (the loop bound is uniform), so the match
-    // below always has the full warp; lanes past the row or outside the prefix take no bin
-    for (int base = 0; base < L; base += kThreads) {
-      const int i = base + threadIdx.x;
-      uint32_t bin = 0xFFFFFFFFu;
-      if (i < L) {
-        const uint32_t key = score_key(__ldg(sr + i));
-        if (pass == 0 || (key >> hsh) == prefix) bin = (key >> sh) & bmask;
-      }
-      // one atomic per distinct bin of the warp
-      const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-      if (bin != 0xFFFFFFFFu && (__ffs(peers) - 1) == lane)
-        atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+  uint32_t* wh = whist[warp];
+  for (int pass = 0; pass < 4; ++pass) {
+    const int sh = 24 - 8 * pass;
+    for (int j = lane; j < kBins; j += 32) wh[j] = 0u;
+    __syncwarp();
+    for (int i = threadIdx.x; i < L; i += kThreads) {
+      const uint32_t key = score_key(__ldg(sr + i));
+      // pass 0 takes every key; later passes the keys whose higher bytes equal the prefix
+      if (pass == 0 || (key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
     }
     __syncthreads();
+    if (threadIdx.x < kBins) {
+      uint32_t c = 0;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) c += whist[w][threadIdx.x];
+      hist[threadIdx.x] = c;
+    }
     if (threadIdx.x == 0) {
       bin_s = -1;
       above_s = 0u;
     }
     __syncthreads();
-    const int b = select_bin(hist, nbins[pass], need, wsum, &above_s, &bin_s);
+    const int b = select_bin(hist, need, wsum, &above_s, &bin_s);
     need -= above_s;
-    prefix = (prefix << (pass == 2 ? 8 : 12)) | (uint32_t)b;
+    prefix = (prefix << 8) | (uint32_t)b;
     __syncthreads();
   }
   const uint32_t T = prefix;  // the k-th largest key; `need` keys equal to T are taken
