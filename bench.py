@@ -332,6 +332,68 @@ def workload_record(name, dev, stream, args, peaks, kernel, read_device_errors):
     return rec
 
 
+# Multi-token rows: the last 128 tokens of 8 sequences (1024 rows of 16 heads), decoded per
+# token (kernel() on each token's selection) and in groups of 8 tokens (union_groups +
+# kernel_grouped).  "all": 2048-token sequences, every token selects all its causal
+# positions (full overlap); "random": 32768-token sequences, 2048 positions per token drawn
+# independently (the least overlap).
+MULTI_TOKEN_CASES = {"prefill_all": dict(seq_len=2048, mode="all"),
+                     "prefill_random": dict(seq_len=32768, mode="random")}
+
+
+def multi_token_record(dev, stream, args, kernel, kernel_grouped, union_groups,
+                       read_device_errors):
+    """Per-token against grouped decode of prefill chunks (one GPU, four rotating sets)."""
+    import torch
+
+    from flashinfer_mlsys2026_dsa_b200 import workloads
+
+    recs = {}
+    for name, cfg in MULTI_TOKEN_CASES.items():
+        sets = [workloads.make_prefill(8, 128, cfg["seq_len"], heads=16, topk=2048,
+                                       mode=cfg["mode"], device=dev, seed=args.seed * 13 + s)
+                for s in range(N_SETS)]
+        B, H = sets[0].num_tokens, sets[0].num_heads
+        G = 128 // H
+        out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+        tables = [w.page_table[::G].contiguous() for w in sets]
+        with torch.cuda.stream(stream):
+            unions = [union_groups(w.positions, t, G) for w, t in zip(sets, tables)]
+        stream.synchronize()
+        reps = max(1, math.ceil(args.steps / N_SETS))
+        wu = max(1, math.ceil(args.warmup / N_SETS))
+        per_token = graph_ms([lambda w=w: kernel(*w.args(), out, lse) for w in sets], reps, wu,
+                             stream)
+        grouped = graph_ms([lambda w=w, u=u: kernel_grouped(w.q_nope, w.q_pe, w.ckv_cache,
+                                                            w.kpe_cache, u[0], u[1], w.sm_scale,
+                                                            out, lse)
+                            for w, u in zip(sets, unions)], reps, wu, stream)
+        union_ms = graph_ms([lambda w=w, t=t: union_groups(w.positions, t, G)
+                             for w, t in zip(sets, tables)], reps, wu, stream)
+        sel = sum(float((w.positions >= 0).sum().item()) for w in sets) / N_SETS
+        uni = sum(float(u[2].sum().item()) for u in unions) / N_SETS
+        rec = {"tokens": B, "heads": H, "group": G, "seq_len": cfg["seq_len"],
+               "selection": cfg["mode"], "topk": 2048,
+               "union_over_selections": round(uni / sel, 4),
+               "per_token_us_per_call": round(per_token * 1e3, 2),
+               "grouped_us_per_call": round(grouped * 1e3, 2),
+               "union_us_per_call": round(union_ms * 1e3, 2),
+               "per_token_us_per_token": round(per_token * 1e3 / B, 4),
+               "grouped_us_per_token": round((grouped + union_ms) * 1e3 / B, 4),
+               "gain": round(per_token / (grouped + union_ms), 3)}
+        with torch.cuda.stream(stream):
+            rec["device_errors"] = read_device_errors(dev)
+        recs[name] = rec
+        del sets, unions, tables, out, lse
+        torch.cuda.empty_cache()
+    recs["method"] = ("per token: kernel() over each token's own selection; grouped: "
+                      "union_groups (union of 8 tokens' selections + membership bytes) then "
+                      "kernel_grouped (one 128-head row per group), both CUDA-graph replayed "
+                      "over 4 rotating input sets; gain = per-token time / (union + grouped)")
+    return recs
+
+
 B2048_MAX_ROWS_PER_CALL = 1024  # a 1024-row shard's page pool is about 82 GB
 
 
@@ -385,8 +447,9 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from flashinfer_mlsys2026_dsa_b200 import (kernel, kernel_paged, read_device_errors,
-                                               topk_slots, workloads)
+    from flashinfer_mlsys2026_dsa_b200 import (kernel, kernel_grouped, kernel_paged,
+                                               read_device_errors, topk_slots, union_groups,
+                                               workloads)
 
     world, rank, local = _dist_setup(args.gpus)
     torch.cuda.set_device(local)
@@ -601,6 +664,10 @@ def run_ours(args):
                                               read_device_errors)
     b2048 = None if args.no_extra else b2048_record(dev, stream, args, peaks, kernel, world,
                                                     rank, barrier)
+    multi = None
+    if world == 1 and not args.no_extra:
+        multi = multi_token_record(dev, stream, args, kernel, kernel_grouped, union_groups,
+                                   read_device_errors)
 
     base = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -650,6 +717,8 @@ def run_ours(args):
         line["workloads"] = extra
     if b2048 is not None:
         line["b2048"] = b2048
+    if multi is not None:
+        line["multi_token"] = multi
     if base is not None:
         line["cpu_baseline"] = base
     print(json.dumps(line), flush=True)

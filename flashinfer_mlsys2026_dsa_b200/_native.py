@@ -45,7 +45,9 @@ EXPORTED_SYMBOLS = (
     "dsa_sparse_mla_decode",
     "dsa_sparse_mla_decode_paged",
     "dsa_sparse_mla_decode_noalloc",
+    "dsa_sparse_mla_decode_grouped",
     "dsa_topk_slots",
+    "dsa_union_groups",
     "dsa_sparse_mla_decode_workspace_size",
     "dsa_read_error_word",
     "dsa_selftest_bounded_wait",
@@ -89,6 +91,18 @@ def load(build_if_missing: bool = True):
                                        _c.c_int64, _c.c_int32, _c.c_int32, _c.c_int64,
                                        _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_int64,
                                        _c.c_void_p]
+        lib.dsa_union_groups.restype = _c.c_int
+        lib.dsa_union_groups.argtypes = [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int32,
+                                         _c.c_int32, _c.c_void_p, _c.c_int64, _c.c_int32,
+                                         _c.c_int32, _c.c_void_p, _c.c_void_p, _c.c_int64,
+                                         _c.c_int32, _c.c_void_p, _c.c_void_p]
+        lib.dsa_sparse_mla_decode_grouped.restype = _c.c_int
+        lib.dsa_sparse_mla_decode_grouped.argtypes = [
+            _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int64,
+            _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int64,
+            _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_float,
+            _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int64,
+            _c.c_int64, _c.c_int32, _c.c_void_p, _c.c_size_t, _c.c_void_p]
         lib.dsa_sparse_mla_decode_workspace_size.restype = _c.c_size_t
         lib.dsa_sparse_mla_decode_workspace_size.argtypes = [_c.c_int64, _c.c_int32, _c.c_int32,
                                                              _c.c_int32]

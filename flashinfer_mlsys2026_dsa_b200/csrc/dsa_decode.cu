@@ -53,6 +53,11 @@ struct Params {
   int64_t pt_sb;
   int32_t pt_cols;
   int32_t pg_shift;  // log2(page_size)
+  // grouped calls only (128-head kernel): a membership byte per index entry, bit j = token
+  // j of the row's token group selected the entry; head h belongs to token h >> tok_shift
+  const uint8_t* member;
+  int64_t member_sb;
+  int32_t tok_shift;
 };
 
 // UMMA shared-memory descriptor, 128-byte swizzle, sm_100 (version 1).
@@ -209,20 +214,22 @@ using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorM
 struct KernelVariant {
   int nh;       // heads per work unit
   bool paged;   // slot ids formed from page tables
+  bool member;  // token groups: entries carry membership bytes
   DecodeKernelFn fn;
   int smem;
 };
 const KernelVariant kVariants[] = {
-    {16, false, h16::dsa_decode_h16_kernel<16, false>, h16::Cfg<16>::SMEM_BYTES},
-    {16, true, h16::dsa_decode_h16_kernel<16, true>, h16::Cfg<16>::SMEM_BYTES},
-    {32, false, h16::dsa_decode_h16_kernel<32, false>, h16::Cfg<32>::SMEM_BYTES},
-    {32, true, h16::dsa_decode_h16_kernel<32, true>, h16::Cfg<32>::SMEM_BYTES},
-    {128, false, hm::dsa_decode_hm_kernel<false>, hm::SMEM_BYTES},
-    {128, true, hm::dsa_decode_hm_kernel<true>, hm::SMEM_BYTES},
+    {16, false, false, h16::dsa_decode_h16_kernel<16, false>, h16::Cfg<16>::SMEM_BYTES},
+    {16, true, false, h16::dsa_decode_h16_kernel<16, true>, h16::Cfg<16>::SMEM_BYTES},
+    {32, false, false, h16::dsa_decode_h16_kernel<32, false>, h16::Cfg<32>::SMEM_BYTES},
+    {32, true, false, h16::dsa_decode_h16_kernel<32, true>, h16::Cfg<32>::SMEM_BYTES},
+    {128, false, false, hm::dsa_decode_hm_kernel<false, false>, hm::SMEM_BYTES},
+    {128, true, false, hm::dsa_decode_hm_kernel<true, false>, hm::SMEM_BYTES},
+    {128, false, true, hm::dsa_decode_hm_kernel<false, true>, hm::SMEM_BYTES},
 };
-const KernelVariant& variant(int nh, bool paged) {
+const KernelVariant& variant(int nh, bool paged, bool member) {
   for (const KernelVariant& kv : kVariants)
-    if (kv.nh == nh && kv.paged == paged) return kv;
+    if (kv.nh == nh && kv.paged == paged && kv.member == member) return kv;
   return kVariants[0];
 }
 // Heads per work unit: 16 for 16-head rows, 32 for 32- and 64-head rows (two units per
@@ -396,6 +403,10 @@ struct DecodeArgs {
   int64_t pt_sb = 0;
   int32_t pt_cols = 0;
   int32_t page_size = 0;
+  // grouped calls (128-head rows made of token groups): membership bytes beside idx
+  const uint8_t* member = nullptr;
+  int64_t member_sb = 0;
+  int32_t tok_shift = 0;
 };
 
 int check_args(const DecodeArgs& a) {
@@ -521,7 +532,10 @@ int run_plan(const DecodeArgs& a, const Plan& pl, uint8_t* ws, cudaStream_t st) 
   prm.pt_cols = a.pt_cols;
   prm.pg_shift = 0;
   while (a.page_table != nullptr && (1 << prm.pg_shift) < a.page_size) ++prm.pg_shift;
-  const KernelVariant& kv = variant(pl.nh, a.page_table != nullptr);
+  prm.member = a.member;
+  prm.member_sb = a.member_sb;
+  prm.tok_shift = a.tok_shift;
+  const KernelVariant& kv = variant(pl.nh, a.page_table != nullptr, a.member != nullptr);
   return launch_pdl(kv.fn, dim3((unsigned)(2 * pl.grid)), dim3(h16::kThreads),
                     (size_t)kv.smem, st, m_ckv, m_kpe, m_qn, m_qp, prm);
 }
@@ -624,6 +638,38 @@ int dsa_sparse_mla_decode_paged(
   a.pt_sb = page_table_stride_b;
   a.pt_cols = page_table_cols;
   a.page_size = page_size;
+  return decode_with_workspace(a, workspace, workspace_bytes, stream);
+}
+
+int dsa_sparse_mla_decode_grouped(
+    const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h, const void* q_pe,
+    int64_t q_pe_stride_b, int64_t q_pe_stride_h, const void* ckv_cache, int64_t ckv_slot_stride,
+    const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots,
+    const int32_t* union_indices, const uint8_t* member, int64_t union_stride_g,
+    int32_t union_cols, float sm_scale, void* output, int64_t output_stride_b,
+    int64_t output_stride_h, float* lse, int64_t lse_stride_b, int64_t lse_stride_h,
+    int64_t num_tokens, int32_t num_heads, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  // A group of G = 128 / num_heads consecutive tokens is one 128-head row: the token's
+  // heads must follow each other in q_nope, q_pe, output and lse (stride_b = num_heads x
+  // stride_h), so that the group's 128 heads are rows of one strided array.
+  if (num_heads != 16 && num_heads != 32 && num_heads != 64) return DSA_ERR_UNSUPPORTED;
+  const int64_t G = 128 / num_heads;
+  if (num_tokens < 0 || num_tokens % G != 0 || union_cols < 1) return DSA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return DSA_OK;
+  if (!union_indices || !member || union_stride_g < union_cols) return DSA_ERR_INVALID_ARGUMENT;
+  if (q_nope_stride_b != num_heads * q_nope_stride_h || q_pe_stride_b != num_heads * q_pe_stride_h ||
+      output_stride_b != num_heads * output_stride_h || lse_stride_b != num_heads * lse_stride_h)
+    return DSA_ERR_INVALID_ARGUMENT;
+  DecodeArgs a{q_nope,          G * q_nope_stride_b, q_nope_stride_h, q_pe,
+               G * q_pe_stride_b, q_pe_stride_h,     ckv_cache,       ckv_slot_stride,
+               kpe_cache,       kpe_slot_stride,     num_slots,       union_indices,
+               union_stride_g,  sm_scale,            output,          G * output_stride_b,
+               output_stride_h, lse,                 G * lse_stride_b, lse_stride_h,
+               num_tokens / G,  128,                 union_cols};
+  a.member = member;
+  a.member_sb = union_stride_g;
+  a.tok_shift = num_heads == 16 ? 4 : (num_heads == 32 ? 5 : 6);
   return decode_with_workspace(a, workspace, workspace_bytes, stream);
 }
 

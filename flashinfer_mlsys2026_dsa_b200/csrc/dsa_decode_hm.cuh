@@ -53,7 +53,8 @@ constexpr int OFF_Q = kStages * kStageB;
 constexpr int OFF_X = OFF_Q + kQB;
 constexpr int OFF_BAR = OFF_X + kXB;
 constexpr int OFF_MASK = OFF_BAR + 512;        // [stage][kMaskStride] slot-validity words
-constexpr int OFF_MISC = OFF_MASK + 128;       // [0] TMEM base, [2] abort, [3] drain, [6] the
+constexpr int OFF_MEMB = OFF_MASK + 128;       // grouped calls: [stage][kTS / 4] membership words
+constexpr int OFF_MISC = OFF_MEMB + 256;       // [0] TMEM base, [2] abort, [3] drain, [6] the
                                                // peer's abort flag (at exit), [8] merge lost
 constexpr int SMEM_USED = OFF_MISC + 64;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;
@@ -100,7 +101,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <bool kPaged>
+// kMember: a grouped call (each row is a group of 128 >> tok_shift tokens over the union of
+// their selections; a membership byte per entry masks the other tokens' heads).
+template <bool kPaged, bool kMember>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     dsa_decode_hm_kernel(const __grid_constant__ CUtensorMap tm_ckv,
                          const __grid_constant__ CUtensorMap tm_kpe,
@@ -117,6 +120,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t peer = rank ^ 1u;
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
   volatile uint32_t* masks = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MASK);
+  volatile uint32_t* memb = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MEMB);
   const uint32_t bar0 = sbase + (uint32_t)OFF_BAR;
 #define bar(k) (bar0 + 8u * (uint32_t)(k))
 
@@ -184,9 +188,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp >= kProd0 && warp < kProd0 + kProdWarps) {
     // ------------------------------------------------------------------ gather producers
     ptx::regs_dec<kRegsLow>();
-    pipe::gather_producer<kTS, kStageB, kStages, kMaskStride, kPaged>(
+    pipe::gather_producer<kTS, kStageB, kStages, kMaskStride, kPaged, kMember>(
         p, &tm_ckv, &tm_kpe, warp - kProd0, lane, rank, sbase + (uint32_t)OFF_KV, masks, bar(B_KVF),
-        bar(B_KVE), u_lo, u_hi, wait, misc + 3);
+        bar(B_KVE), u_lo, u_hi, wait, misc + 3, memb);
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ score MMA issuer
@@ -550,15 +554,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const bool live = masks[st * kMaskStride + kMaskAny] != 0u;
         float x[64];
         float mt = -INFINITY;
+        const int tok = kMember ? (h >> p.tok_shift) : 0;  // this head's token in the group
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const float4 v = *reinterpret_cast<const float4*>(sgen + OFF_X + xoff(h, c));
           const float pv[4] = {v.x, v.y, v.z, v.w};
+          const uint32_t mb = kMember ? memb[st * (kTS / 4) + c] >> tok : 0u;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int k = 4 * c + e;
             const uint32_t ob = k < 32 ? own0[k] : own1[k - 32];
-            const bool valid = ((k < 32 ? mw0 >> k : mw1 >> (k - 32)) & 1u) != 0u;
+            const bool valid = ((k < 32 ? mw0 >> k : mw1 >> (k - 32)) & 1u) != 0u &&
+                               (!kMember || ((mb >> (8 * e)) & 1u) != 0u);
             x[k] = valid ? (__uint_as_float(ob) + pv[e]) * p.scale_log2 : -INFINITY;
             mt = fmaxf(mt, x[k]);
           }

@@ -72,13 +72,20 @@ __device__ __forceinline__ void translate(const Params& p, int64_t rh, const int
 // valid) and flags bad indices.  kPaged: the entries are token positions, fetched two tiles
 // ahead and translated through the row's page table one tile ahead, so the dependent
 // page-table load is off the producer's path.
-template <int kTS, int kStageB, int kStages, int kMaskStride, bool kPaged>
+//
+// kMember (token groups): d-block 0's warp also loads the entries' membership bytes one
+// tile ahead, like the ids, and stores them per stage into `memb` ([kStages][kTS / 4]
+// words, byte e of word g = entry 4g + e, zero for padding and bad entries) before the
+// stage's full barrier is armed.
+template <int kTS, int kStageB, int kStages, int kMaskStride, bool kPaged, bool kMember = false>
 __device__ __forceinline__ void gather_producer(const Params& p, const CUtensorMap* tm_ckv,
                                                 const CUtensorMap* tm_kpe, int blk, int lane,
                                                 uint32_t rank, uint32_t stage0,
                                                 volatile uint32_t* masks, uint32_t kvf0,
                                                 uint32_t kve0, int64_t u_lo, int64_t u_hi,
-                                                const Waiter& wait, volatile uint32_t* drain_flag) {
+                                                const Waiter& wait, volatile uint32_t* drain_flag,
+                                                volatile uint32_t* memb = nullptr) {
+  static_assert(!(kMember && kPaged), "membership bytes come with flat slot ids");
   constexpr int kRB = kTS * 128;  // one ckv d-block region of a stage
   constexpr int kGroups = kTS / 4;
   static_assert(kGroups <= 32 && kTS <= 128, "one gather4 group per lane, four mask words");
@@ -108,8 +115,25 @@ __device__ __forceinline__ void gather_producer(const Params& p, const CUtensorM
         asm volatile("prefetch.global.L2 [%0];" ::"l"(pr + c));
     }
   };
+  // membership bytes of a lane's four entries (d-block 0's warp of a grouped call)
+  auto tile_member = [&](int64_t rh, int t) -> uint32_t {
+    uint32_t m = 0;
+    if constexpr (kMember) {
+      if (blk == 0 && has) {
+        const uint8_t* mr = p.member + rh * p.member_sb;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = t * kTS + 4 * g + e;
+          if (k < p.topk) m |= (uint32_t)__ldg(mr + k) << (8 * e);
+        }
+      }
+    }
+    return m;
+  };
+  uint32_t mcur = 0, mnxt = 0;
   if (u_lo < u_hi) pf_row(n_rh);
   if (u_lo < u_hi) {
+    if constexpr (kMember) mcur = tile_member(n_rh, n_t);
     tile_entries<kTS>(p, n_rh, n_t, has, g, kPaged ? ahead : cur);
     if constexpr (kPaged) translate(p, n_rh, ahead, cur);
   }
@@ -138,7 +162,10 @@ __device__ __forceinline__ void gather_producer(const Params& p, const CUtensorM
       a_rh = n_rh;
       if (uu + 2 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, ahead);
     } else {
-      if (uu + 1 < u_hi) tile_entries<kTS>(p, n_rh, n_t, has, g, nxt);
+      if (uu + 1 < u_hi) {
+        if constexpr (kMember) mnxt = tile_member(n_rh, n_t);
+        tile_entries<kTS>(p, n_rh, n_t, has, g, nxt);
+      }
     }
     uint32_t nib = 0;
     bool bad = false;
@@ -166,21 +193,48 @@ __device__ __forceinline__ void gather_producer(const Params& p, const CUtensorM
       w2 = __reduce_or_sync(0xffffffffu, (g >> 3) == 2 ? sh : 0u);
       w3 = __reduce_or_sync(0xffffffffu, (g >> 3) == 3 ? sh : 0u);
     }
-    if (lane == 0) {
-      ok = wait(kve0 + 8u * (uint32_t)(5 * st + blk), phase ^ 1u);
-      if (ok) {
+    if constexpr (kMember) {
+      // the stage's region must be free before its membership words are rewritten: the
+      // whole warp learns the outcome of the wait first
+      if (lane == 0) ok = wait(kve0 + 8u * (uint32_t)(5 * st + blk), phase ^ 1u);
+      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+      if (!ok) break;
+      if (blk == 0 && has) {
+        uint32_t mw = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (cur[e] >= 0) mw |= mcur & (0xFFu << (8 * e));
+        memb[st * (kTS / 4) + g] = mw;
+      }
+      __syncwarp();
+      if (lane == 0) {
         if (blk == 0) {
           masks[st * kMaskStride + 0] = w0;
           masks[st * kMaskStride + 1] = w1;
           masks[st * kMaskStride + 2] = w2;
           masks[st * kMaskStride + 3] = w3;
-          masks[st * kMaskStride + kMaskAny] = w0 | w1 | w2 | w3;  // nonzero: a valid slot
+          masks[st * kMaskStride + kMaskAny] = w0 | w1 | w2 | w3;
         }
         ptx::mbar_arrive_expect_tx(kvf0 + 8u * (uint32_t)st, n_req * req_bytes);
       }
+      mcur = mnxt;
+    } else {
+      if (lane == 0) {
+        ok = wait(kve0 + 8u * (uint32_t)(5 * st + blk), phase ^ 1u);
+        if (ok) {
+          if (blk == 0) {
+            masks[st * kMaskStride + 0] = w0;
+            masks[st * kMaskStride + 1] = w1;
+            masks[st * kMaskStride + 2] = w2;
+            masks[st * kMaskStride + 3] = w3;
+            masks[st * kMaskStride + kMaskAny] = w0 | w1 | w2 | w3;  // nonzero: a valid slot
+          }
+          ptx::mbar_arrive_expect_tx(kvf0 + 8u * (uint32_t)st, n_req * req_bytes);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+      if (!ok) break;
     }
-    ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
-    if (!ok) break;
     n_issued = i + 1;
     if (issue)
       ptx::tma_gather4(stage0 + (uint32_t)(st * kStageB) + dst_off, map, col,

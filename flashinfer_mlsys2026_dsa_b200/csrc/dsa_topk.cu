@@ -10,6 +10,9 @@
 // the row's positions when the row has fewer than k (the decode's padding), so that the
 // result is one deterministic array.
 //
+// Without a page table the output is the selected positions themselves (the input of the
+// token-group union below).
+//
 // One CTA per row (1024 threads).  Scores are mapped to order-preserving 32-bit keys; a
 // radix select finds the k-th largest key T in four histogram passes over the key's bytes,
 // high to low (each later pass only over the keys that share the bytes already fixed), with
@@ -19,6 +22,8 @@
 // coalesced, so positions come out in order without a sort.
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <atomic>
 
 #include "dsa_b200.h"
 
@@ -51,6 +56,7 @@ __device__ __forceinline__ uint32_t score_key(float f) {
 }
 
 __device__ __forceinline__ int32_t slot_of(const Params& p, const int32_t* pr, int pos) {
+  if (pr == nullptr) return pos;  // no page table: the positions themselves
   const int pg = pos >> p.pg_shift;
   if (pg >= p.pt_cols) return -1;
   const int32_t page = __ldg(pr + pg);
@@ -112,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   const int row = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* sr = p.scores + (int64_t)row * p.scores_sb;
-  const int32_t* pr = p.pt + (int64_t)row * p.pt_sb;
+  const int32_t* pr = p.pt ? p.pt + (int64_t)row * p.pt_sb : nullptr;
   int32_t* out = p.slots + (int64_t)row * p.slots_sb;
   int L = __ldg(p.lengths + row);
   L = L < 0 ? 0 : (L > p.max_len ? p.max_len : L);
@@ -195,6 +201,107 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Union of the selections of a token group, for the grouped decode.
+//
+// G consecutive tokens of one sequence (G * heads = 128) are decoded as one 128-head row
+// over the union of their selected positions: each union entry is gathered once for all
+// G tokens and carries a membership byte (bit j: token j of the group selected it), which
+// masks the other tokens' heads in the softmax.  One CTA per group: the positions of the
+// group's tokens are scattered into a membership byte per position in shared memory (one
+// window of kWin positions at a time), then an ordered compaction writes the positions
+// that any token selected, ascending, translated through the group's page table (a
+// position past the table or on a negative page becomes a -1 entry with no member), -1 /
+// 0 after the last entry.  counts[g] receives the union size; entries past out_cols are
+// dropped (counts[g] > out_cols tells the caller).
+
+constexpr int kWin = 65536;            // positions per shared-memory window (64 KB)
+constexpr int kWinWords = kWin / 4;    // membership bytes packed four to a word
+constexpr int kWordsPerThread = kWinWords / kThreads;
+
+struct UnionParams {
+  const int32_t* pos;
+  int64_t pos_sb;
+  int32_t k;
+  int32_t group;
+  const int32_t* pt;
+  int64_t pt_sb;
+  int32_t pt_cols;
+  int32_t pg_shift;
+  int64_t max_pos;  // pt_cols * page_size
+  int32_t* slots;
+  uint8_t* member;
+  int64_t out_sb;
+  int32_t out_cols;
+  int32_t* counts;
+};
+
+// Nonzero bytes of a word, as a 4-bit mask (bit b: byte b is nonzero).
+__device__ __forceinline__ uint32_t nonzero_bytes(uint32_t v) {
+  return (v & 0xFFu ? 1u : 0u) | (v & 0xFF00u ? 2u : 0u) | (v & 0xFF0000u ? 4u : 0u) |
+         (v & 0xFF000000u ? 8u : 0u);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) union_groups_kernel(const UnionParams p) {
+  extern __shared__ uint32_t win[];  // kWinWords membership words
+  __shared__ uint32_t wsum[32];
+  __shared__ uint32_t total_s;
+  const int g = blockIdx.x;
+  const int32_t* pr = p.pt + (int64_t)g * p.pt_sb;
+  int32_t* so = p.slots + (int64_t)g * p.out_sb;
+  uint8_t* mo = p.member + (int64_t)g * p.out_sb;
+  const int mask = (1 << p.pg_shift) - 1;
+  int64_t n_out = 0;  // union entries so far (block-uniform)
+  for (int64_t w0 = 0; w0 < p.max_pos; w0 += kWin) {
+    for (int i = threadIdx.x; i < kWinWords; i += kThreads) win[i] = 0u;
+    __syncthreads();
+    for (int j = 0; j < p.group; ++j) {
+      const int32_t* pj = p.pos + ((int64_t)g * p.group + j) * p.pos_sb;
+      for (int i = threadIdx.x; i < p.k; i += kThreads) {
+        const int64_t q = (int64_t)__ldg(pj + i) - w0;
+        if (q >= 0 && q < kWin && q + w0 < p.max_pos)
+          atomicOr(&win[q >> 2], (1u << j) << (8 * (int)(q & 3)));
+      }
+    }
+    __syncthreads();
+    // thread t owns words [t * kWordsPerThread, (t + 1) * kWordsPerThread) of the window
+    const int wbase = threadIdx.x * kWordsPerThread;
+    uint32_t cnt = 0;
+#pragma unroll 8
+    for (int i = 0; i < kWordsPerThread; ++i) cnt += __popc(nonzero_bytes(win[wbase + i]));
+    const uint32_t incl = block_inclusive_scan(cnt, wsum);
+    if (threadIdx.x == kThreads - 1) total_s = incl;
+    int64_t o = n_out + (int64_t)(incl - cnt);
+    for (int i = 0; i < kWordsPerThread; ++i) {
+      const uint32_t v = win[wbase + i];
+      if (v == 0u) continue;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t m = (v >> (8 * b)) & 0xFFu;
+        if (m == 0u) continue;
+        if (o < p.out_cols) {
+          const int64_t q = w0 + 4 * (int64_t)(wbase + i) + b;
+          const int pg = (int)(q >> p.pg_shift);
+          const int32_t page = pg < p.pt_cols ? __ldg(pr + pg) : -1;
+          const int64_t slot = page < 0 ? -1 : (((int64_t)page << p.pg_shift) | (q & mask));
+          const bool ok = slot >= 0 && slot <= (int64_t)INT32_MAX;
+          so[o] = ok ? (int32_t)slot : -1;
+          mo[o] = ok ? (uint8_t)m : (uint8_t)0;
+        }
+        ++o;
+      }
+    }
+    __syncthreads();
+    n_out += total_s;
+    __syncthreads();  // total_s and win are rewritten by the next window
+  }
+  for (int64_t i = n_out + threadIdx.x; i < p.out_cols; i += kThreads) {
+    so[i] = -1;
+    mo[i] = 0;
+  }
+  if (threadIdx.x == 0 && p.counts) p.counts[g] = (int32_t)(n_out < INT32_MAX ? n_out : INT32_MAX);
+}
+
 }  // namespace topk
 }  // namespace dsa
 
@@ -205,11 +312,11 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
                               int64_t slots_stride_b, void* stream) {
   if (num_rows < 0 || max_len < 0 || k < 1 || num_rows > INT32_MAX) return DSA_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return DSA_OK;
-  if (!scores || !lengths || !page_table || !slots) return DSA_ERR_INVALID_ARGUMENT;
-  if (scores_stride_b < max_len || slots_stride_b < k || page_table_cols < 1 ||
-      page_table_stride_b < page_table_cols)
-    return DSA_ERR_INVALID_ARGUMENT;
-  if (page_size < 1 || page_size > (1 << 20) || (page_size & (page_size - 1)) != 0)
+  if (!scores || !lengths || !slots) return DSA_ERR_INVALID_ARGUMENT;
+  if (scores_stride_b < max_len || slots_stride_b < k) return DSA_ERR_INVALID_ARGUMENT;
+  if (page_table != nullptr &&
+      (page_table_cols < 1 || page_table_stride_b < page_table_cols || page_size < 1 ||
+       page_size > (1 << 20) || (page_size & (page_size - 1)) != 0))
     return DSA_ERR_INVALID_ARGUMENT;
   dsa::topk::Params p;
   p.scores = scores;
@@ -219,12 +326,60 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
   p.pt_sb = page_table_stride_b;
   p.pt_cols = page_table_cols;
   p.pg_shift = 0;
-  while ((1 << p.pg_shift) < page_size) ++p.pg_shift;
+  while (page_table != nullptr && (1 << p.pg_shift) < page_size) ++p.pg_shift;
   p.max_len = max_len;
   p.k = k;
   p.slots = slots;
   p.slots_sb = slots_stride_b;
   dsa::topk::topk_slots_kernel<<<(unsigned)num_rows, dsa::topk::kThreads, 0,
                                  static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+extern "C" int dsa_union_groups(const int32_t* positions, int64_t positions_stride_b,
+                                int64_t num_tokens, int32_t k, int32_t group,
+                                const int32_t* page_table, int64_t page_table_stride_g,
+                                int32_t page_table_cols, int32_t page_size, int32_t* slots,
+                                uint8_t* member, int64_t out_stride_g, int32_t out_cols,
+                                int32_t* counts, void* stream) {
+  if (num_tokens < 0 || k < 1 || group < 1 || group > 8 || out_cols < 1 ||
+      num_tokens % group != 0 || num_tokens / group > INT32_MAX)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return DSA_OK;
+  if (!positions || !page_table || !slots || !member) return DSA_ERR_INVALID_ARGUMENT;
+  if (positions_stride_b < k || out_stride_g < out_cols || page_table_cols < 1 ||
+      page_table_stride_g < page_table_cols || page_size < 1 || page_size > (1 << 20) ||
+      (page_size & (page_size - 1)) != 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  dsa::topk::UnionParams p;
+  p.pos = positions;
+  p.pos_sb = positions_stride_b;
+  p.k = k;
+  p.group = group;
+  p.pt = page_table;
+  p.pt_sb = page_table_stride_g;
+  p.pt_cols = page_table_cols;
+  p.pg_shift = 0;
+  while ((1 << p.pg_shift) < page_size) ++p.pg_shift;
+  p.max_pos = (int64_t)page_table_cols * page_size;
+  p.slots = slots;
+  p.member = member;
+  p.out_sb = out_stride_g;
+  p.out_cols = out_cols;
+  p.counts = counts;
+  constexpr int kSmem = dsa::topk::kWinWords * 4;
+  // the shared-memory limit is a per-device function attribute: set once per device (not
+  // inside a stream capture when the first call ran eagerly)
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSA_ERR_CUDA;
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(dsa::topk::union_groups_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    attr_set[dev].store(true, std::memory_order_release);
+  }
+  dsa::topk::union_groups_kernel<<<(unsigned)(num_tokens / group), dsa::topk::kThreads, kSmem,
+                                   static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }

@@ -89,7 +89,8 @@ _BF16 = torch.bfloat16
 _REVALIDATE = (-1, 1, 2)
 
 
-def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
+def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse,
+              check_index_rows=True):
     tensors = (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache),
                ("kpe_cache", kpe_cache), ("sparse_indices", sparse_indices), ("output", output),
                ("lse", lse))
@@ -117,7 +118,7 @@ def _validate(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, output, lse):
         raise ValueError(f"q_pe must be [{B}, {H}, {D_KPE}], got {tuple(q_pe.shape)}")
     if ckv_cache.shape[-1] != D_CKV or kpe_cache.shape[-1] != D_KPE:
         raise ValueError("ckv_cache / kpe_cache last dims must be 512 / 64")
-    if sparse_indices.dim() != 2 or sparse_indices.shape[0] != B:
+    if sparse_indices.dim() != 2 or (check_index_rows and sparse_indices.shape[0] != B):
         raise ValueError(f"sparse_indices must be [{B}, topk], got {tuple(sparse_indices.shape)}")
     if output.shape != (B, H, D_CKV):
         raise ValueError(f"output must be [{B}, {H}, {D_CKV}], got {tuple(output.shape)}")
@@ -291,17 +292,20 @@ def topk_slots(scores, lengths, page_table, k, page_size=PAGE_SIZE, out=None):
     side (solution/triton/baseline.py:17-23); flashinfer names the step
     ``top_k_page_table_transform``.
     """
-    for name, t in (("scores", scores), ("lengths", lengths), ("page_table", page_table)):
+    tensors = (("scores", scores), ("lengths", lengths))
+    if page_table is not None:
+        tensors += (("page_table", page_table),)
+    for name, t in tensors:
         if not isinstance(t, torch.Tensor) or not t.is_cuda:
             raise ValueError(f"{name} must be a CUDA tensor")
     if scores.dtype != torch.float32:
         raise TypeError(f"scores must be float32, got {scores.dtype}")
-    if lengths.dtype != torch.int32 or page_table.dtype != torch.int32:
+    if lengths.dtype != torch.int32 or (page_table is not None and page_table.dtype != torch.int32):
         raise TypeError("lengths and page_table must be int32")
-    if scores.dim() != 2 or page_table.dim() != 2:
+    if scores.dim() != 2 or (page_table is not None and page_table.dim() != 2):
         raise ValueError("scores and page_table must be 2-D")
     rows, max_len = scores.shape
-    if lengths.shape != (rows,) or page_table.shape[0] != rows:
+    if lengths.shape != (rows,) or (page_table is not None and page_table.shape[0] != rows):
         raise ValueError("lengths must be [rows] and page_table [rows, max_pages]")
     k = int(k)
     page_size = int(page_size)
@@ -309,7 +313,7 @@ def topk_slots(scores, lengths, page_table, k, page_size=PAGE_SIZE, out=None):
         raise ValueError("k must be >= 1 and page_size a power of two")
     if scores.stride(-1) != 1:
         scores = scores.contiguous()
-    if page_table.stride(-1) != 1:
+    if page_table is not None and page_table.stride(-1) != 1:
         page_table = page_table.contiguous()
     lengths = lengths.contiguous()
     if out is None:
@@ -318,11 +322,120 @@ def topk_slots(scores, lengths, page_table, k, page_size=PAGE_SIZE, out=None):
         raise ValueError(f"out must be an int32 [{rows}, {k}] tensor with a unit inner stride")
     stream = torch._C._cuda_getCurrentRawStream(scores.get_device())
     lib = _native._lib or _native.load()
+    pt_ptr, pt_sb, pt_cols = ((page_table.data_ptr(), page_table.stride(0), page_table.shape[1])
+                              if page_table is not None else (None, 0, 0))
     _check(lib.dsa_topk_slots(scores.data_ptr(), scores.stride(0), lengths.data_ptr(),
-                              page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
-                              page_size, rows, max_len, k, out.data_ptr(), out.stride(0), stream),
+                              pt_ptr, pt_sb, pt_cols, page_size, rows, max_len, k,
+                              out.data_ptr(), out.stride(0), stream),
            "dsa_topk_slots")
     return out
+
+
+def union_groups(positions, page_table, group, out_cols=None, page_size=PAGE_SIZE):
+    """Union of the selections of token groups, for :func:`kernel_grouped`.
+
+    ``positions`` [tokens, k] int32 CUDA tensor: each token's selected positions (distinct;
+    -1 = none), e.g. :func:`topk_slots` with ``page_table=None``. Tokens ``[g * group,
+    (g + 1) * group)`` form group g and share the sequence's ``page_table`` row g
+    ([tokens // group, max_pages] int32). Returns ``(slots, member, counts)``: per group
+    the union's slot ids in ascending position order then -1 ([groups, out_cols] int32),
+    the membership bytes (bit j: token j of the group selected the entry; uint8, same
+    shape) and the union sizes ([groups] int32). ``out_cols`` defaults to ``min(group * k,
+    max_pages * page_size)``, which always holds the union; a smaller value cuts it
+    (``counts`` shows by how much). One launch on the current stream.
+    """
+    for name, t in (("positions", positions), ("page_table", page_table)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if t.dtype != torch.int32:
+            raise TypeError(f"{name} must be int32, got {t.dtype}")
+        if t.dim() != 2:
+            raise ValueError(f"{name} must be 2-D")
+    group = int(group)
+    tokens, k = positions.shape
+    if group < 1 or group > 8 or tokens % group:
+        raise ValueError(f"group must be in [1, 8] and divide the token count {tokens}")
+    groups = tokens // group
+    if page_table.shape[0] != groups:
+        raise ValueError(f"page_table must be [{groups}, max_pages], got {tuple(page_table.shape)}")
+    page_size = int(page_size)
+    if page_size < 1 or page_size & (page_size - 1):
+        raise ValueError(f"page_size must be a power of two, got {page_size}")
+    if out_cols is None:
+        out_cols = min(group * k, page_table.shape[1] * page_size)
+    out_cols = int(out_cols)
+    if out_cols < 1:
+        raise ValueError("out_cols must be >= 1")
+    positions = positions.contiguous()
+    page_table = page_table.contiguous()
+    dev = positions.device
+    slots = torch.empty(groups, out_cols, dtype=torch.int32, device=dev)
+    member = torch.empty(groups, out_cols, dtype=torch.uint8, device=dev)
+    counts = torch.empty(groups, dtype=torch.int32, device=dev)
+    if groups == 0:
+        return slots, member, counts
+    stream = torch._C._cuda_getCurrentRawStream(positions.get_device())
+    lib = _native._lib or _native.load()
+    _check(lib.dsa_union_groups(positions.data_ptr(), positions.stride(0), tokens, k, group,
+                                page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+                                page_size, slots.data_ptr(), member.data_ptr(), slots.stride(0),
+                                out_cols, counts.data_ptr(), stream),
+           "dsa_union_groups")
+    return slots, member, counts
+
+
+def kernel_grouped(q_nope, q_pe, ckv_cache, kpe_cache, union_indices, member, sm_scale,
+                   output, lse):
+    """Multi-token rows decoded in token groups (prefill chunks, multi-token decode).
+
+    The same result as :func:`kernel` on each token's own selection, computed for groups of
+    ``G = 128 // num_heads`` consecutive tokens of one sequence at once: ``union_indices``
+    and ``member`` [tokens // G, U] (from :func:`union_groups`) hold the union of the
+    group's selections and which token selected each entry, so every union slot is
+    gathered once for the whole group and decoded as one 128-head row. The tokens' heads
+    must be consecutive in ``q_nope``, ``q_pe``, ``output`` and ``lse`` (contiguous
+    [tokens, H, ...] tensors). Pays when the group's selections overlap: the union of G
+    tokens costs about as much as G / 3 separate tokens' selections per slot.
+    """
+    _validate(q_nope, q_pe, ckv_cache, kpe_cache, union_indices, output, lse,
+              check_index_rows=False)
+    B, H, _ = q_nope.shape
+    if H not in (16, 32, 64):
+        raise ValueError(f"grouped decode takes 16, 32 or 64 heads per token, got {H}")
+    G = 128 // H
+    if B % G:
+        raise ValueError(f"the token count {B} is not a multiple of the group size {G}")
+    if not isinstance(member, torch.Tensor) or member.dtype != torch.uint8 or \
+            member.shape != union_indices.shape or member.device != union_indices.device:
+        raise ValueError("member must be a uint8 tensor shaped like union_indices, on its device")
+    if union_indices.shape[0] != B // G:
+        raise ValueError(f"union_indices must be [{B // G}, U], got {tuple(union_indices.shape)}")
+    if B == 0:
+        return
+    union_indices = union_indices.contiguous()
+    member = member.contiguous()
+    for name, t in (("q_nope", q_nope), ("q_pe", q_pe), ("output", output), ("lse", lse)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous for the grouped decode")
+    ckv = _slot_view(ckv_cache, D_CKV, "ckv_cache")
+    kpe = _slot_view(kpe_cache, D_KPE, "kpe_cache")
+    if ckv.shape[0] != kpe.shape[0]:
+        raise ValueError("ckv_cache and kpe_cache hold different slot counts")
+    lib = _native._lib or _native.load()
+    stream = torch._C._cuda_getCurrentRawStream(q_nope.get_device())
+    U = union_indices.shape[1]
+    ws = workspace_for(q_nope.device, stream, B // G, 128, U)
+    rc = lib.dsa_sparse_mla_decode_grouped(
+        q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1),
+        q_pe.data_ptr(), q_pe.stride(0), q_pe.stride(1),
+        ckv.data_ptr(), ckv.stride(0), kpe.data_ptr(), kpe.stride(0), ckv.shape[0],
+        union_indices.data_ptr(), member.data_ptr(), union_indices.stride(0), U,
+        float(sm_scale), output.data_ptr(), output.stride(0), output.stride(1),
+        lse.data_ptr(), lse.stride(0), lse.stride(1), B, H,
+        ws.data_ptr(), ws.numel(), stream)
+    _check(rc, "dsa_sparse_mla_decode_grouped")
+    if _strict:
+        _strict_check(q_nope.device, "dsa_sparse_mla_decode_grouped")
 
 
 def decode(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale):

@@ -173,3 +173,66 @@ def make(name: str, device="cuda", seed: int = 0, rank: int = 0, world_size: int
                              torch.full((B, maxp), -1, dtype=perm.dtype, device=device))
     return Workload(name, q_nope, q_pe, ckv, kpe, slots.contiguous(), 1.0 / math.sqrt(192.0), seq,
                     page_table.to(torch.int32).contiguous(), pos.to(torch.int32).contiguous())
+
+
+def make_prefill(num_seqs: int, chunk: int, seq_len: int, heads: int = 16, topk: int = 2048,
+                 mode: str = "all", device="cuda", seed: int = 0) -> Workload:
+    """Multi-token rows: the last ``chunk`` tokens of ``num_seqs`` sequences of ``seq_len``.
+
+    Token j of a sequence sits at position p = seq_len - chunk + j and selects among the
+    positions <= p (causal): every one of them (``mode="all"``, the indexer's choice when
+    the sequence is no longer than topk, so seq_len <= topk), or ``min(topk, p + 1)``
+    distinct ones drawn uniformly and independently per token (``mode="random"``: the
+    least overlap between tokens). Positions are ascending with -1 after them, as the
+    top-k step writes them. Rows are the tokens, sequence by sequence; ``page_table`` has
+    one row per token (equal rows within a sequence).
+    """
+    if mode == "all" and seq_len > topk:
+        raise ValueError("mode 'all' needs seq_len <= topk")
+    device = torch.device(device)
+    gen = torch.Generator().manual_seed(seed * 7919 + 3)
+    gen_dev = torch.Generator(device=device).manual_seed(seed * 7919 + 5)
+    B = num_seqs * chunk
+    npg = -(-seq_len // PAGE)
+    P = num_seqs * npg
+    perm = torch.randperm(P, generator=gen).to(device)
+    seq_pt = perm.view(num_seqs, npg)
+    page_table = seq_pt.repeat_interleave(chunk, dim=0).to(torch.int32).contiguous()
+    p_tok = (seq_len - chunk + torch.arange(chunk, device=device)).repeat(num_seqs)  # [B]
+    ar = torch.arange(seq_len, device=device)
+    pos = torch.full((B, topk), -1, dtype=torch.int64, device=device)
+    rows_per = max(1, (1 << 25) // seq_len)
+    for r0 in range(0, B, rows_per):
+        r1 = min(B, r0 + rows_per)
+        live = ar[None, :] <= p_tok[r0:r1, None]
+        if mode == "all":
+            cand = torch.where(live, ar[None, :].expand(r1 - r0, -1), torch.full_like(ar, seq_len)[None, :])
+            sel = torch.sort(cand, dim=1).values[:, :topk]
+        elif mode == "random":
+            keys = torch.rand(r1 - r0, seq_len, generator=gen_dev, device=device)
+            keys = torch.where(live, keys, torch.full_like(keys, 2.0))
+            k = min(topk, seq_len)
+            v, i = torch.topk(keys, k, dim=1, largest=False)
+            cand = torch.where(v < 2.0, i, torch.full_like(i, seq_len))
+            sel = torch.sort(cand, dim=1).values
+        else:
+            raise ValueError(f"unknown mode {mode!r}")
+        sel = torch.where(sel < seq_len, sel, torch.full_like(sel, -1))
+        pos[r0:r1, :sel.shape[1]] = sel
+    seq_of = torch.arange(B, device=device) // chunk
+    valid = pos >= 0
+    posc = pos.clamp(min=0)
+    page = seq_pt[seq_of[:, None], posc // PAGE]
+    slots = torch.where(valid, page * PAGE + posc % PAGE, torch.full_like(posc, -1)).to(torch.int32)
+
+    def normal(shape, scale):
+        t = torch.randn(shape, generator=gen_dev, device=device, dtype=torch.bfloat16)
+        return t.mul_(scale) if scale != 1.0 else t
+
+    q_nope = normal((B, heads, D_CKV), 1.0)
+    q_pe = normal((B, heads, D_KPE), 1.0)
+    ckv = normal((P, PAGE, D_CKV), 0.5)
+    kpe = normal((P, PAGE, D_KPE), 0.5)
+    return Workload(f"prefill_{mode}", q_nope, q_pe, ckv, kpe, slots.contiguous(),
+                    1.0 / math.sqrt(192.0), [seq_len] * num_seqs, page_table,
+                    pos.to(torch.int32).contiguous())

@@ -130,14 +130,68 @@ int dsa_sparse_mla_decode_paged(
  * Row b gets the slots of its k largest scores (ties at the k-th largest go to the smaller
  * positions; scores are ordered by their IEEE-754 bit pattern: -0.0 below +0.0, NaN below
  * every number), in ascending position order, then -1 up to k when the row has fewer than
- * k positions.  A position past the row's table or on a negative page gives -1.  The
- * result is exact and deterministic.  One launch on `stream`; nothing is allocated.
+ * k positions.  A position past the row's table or on a negative page gives -1.  With
+ * page_table NULL the selected positions themselves are written (page_table_cols and
+ * page_size are then ignored).  The result is exact and deterministic.  One launch on
+ * `stream`; nothing is allocated.
  */
 int dsa_topk_slots(const float* scores, int64_t scores_stride_b, const int32_t* lengths,
                    const int32_t* page_table, int64_t page_table_stride_b,
                    int32_t page_table_cols, int32_t page_size, int64_t num_rows,
                    int32_t max_len, int32_t k, int32_t* slots, int64_t slots_stride_b,
                    void* stream);
+
+/*
+ * Multi-token rows (prefill chunks, multi-token decode) decoded in token groups.
+ *
+ * The reference's operator takes one row per token (fused.py:150; the definition counts
+ * num_tokens, each with its own selection), so consecutive tokens of one sequence gather
+ * the slots they both selected once each.  A token group of G = 128 / num_heads
+ * consecutive tokens of one sequence is decoded here as one 128-head row over the union
+ * of the tokens' selections: each union entry is gathered once for all G tokens, and a
+ * membership byte per entry (bit j: token j of the group selected it) masks the other
+ * tokens' heads.  Every token's output equals the decode of its own selection
+ * (baseline.py:17-45) up to floating-point summation order.
+ *
+ * dsa_union_groups builds the union: positions [num_tokens, >= k] int32 (row stride
+ * positions_stride_b; each token's selected positions, distinct, -1 = none; the output of
+ * dsa_topk_slots with page_table NULL) -> per group g = tokens [g G, (g + 1) G):
+ *   slots  [num_tokens / G, >= out_cols] int32 (row stride out_stride_g): the slot ids of
+ *          the union's positions, ascending by position, translated through the group's
+ *          page table row (page_table [num_tokens / G, >= page_table_cols], page_size a
+ *          power of two; a position past the table or on a negative page becomes -1),
+ *          then -1;
+ *   member [num_tokens / G, >= out_cols] uint8 (same row stride): the membership bytes,
+ *          0 after the union;
+ *   counts [num_tokens / G] int32 (optional, may be NULL): the union sizes.  A union
+ *          larger than out_cols is cut at out_cols (counts shows it); out_cols =
+ *          min(G * k, page_table_cols * page_size) always suffices.
+ * 1 <= G <= 8.  Positions < 0 or >= page_table_cols * page_size are not part of the union.
+ * One launch (one CTA per group) on `stream`; nothing is allocated.
+ *
+ * dsa_sparse_mla_decode_grouped decodes num_tokens tokens of num_heads (16, 32 or 64)
+ * heads as num_tokens / G rows of 128 heads: union_indices and member as written by
+ * dsa_union_groups (union_cols entries per group, row stride union_stride_g for both).
+ * Arguments otherwise as dsa_sparse_mla_decode, with every token's heads consecutive in
+ * q_nope, q_pe, output and lse (stride_b = num_heads * stride_h; output and its strides
+ * 16-byte aligned); num_tokens a multiple of G.  A token with no member entry gets
+ * output 0 and lse -inf, like an all-padding row.
+ */
+int dsa_union_groups(const int32_t* positions, int64_t positions_stride_b, int64_t num_tokens,
+                     int32_t k, int32_t group, const int32_t* page_table,
+                     int64_t page_table_stride_g, int32_t page_table_cols, int32_t page_size,
+                     int32_t* slots, uint8_t* member, int64_t out_stride_g, int32_t out_cols,
+                     int32_t* counts, void* stream);
+
+int dsa_sparse_mla_decode_grouped(
+    const void* q_nope, int64_t q_nope_stride_b, int64_t q_nope_stride_h, const void* q_pe,
+    int64_t q_pe_stride_b, int64_t q_pe_stride_h, const void* ckv_cache, int64_t ckv_slot_stride,
+    const void* kpe_cache, int64_t kpe_slot_stride, int64_t num_slots,
+    const int32_t* union_indices, const uint8_t* member, int64_t union_stride_g,
+    int32_t union_cols, float sm_scale, void* output, int64_t output_stride_b,
+    int64_t output_stride_h, float* lse, int64_t lse_stride_b, int64_t lse_stride_h,
+    int64_t num_tokens, int32_t num_heads, void* workspace, size_t workspace_bytes,
+    void* stream);
 
 /*
  * Bytes of workspace dsa_sparse_mla_decode() needs for this problem on

@@ -228,3 +228,40 @@ def topk_slots_numpy(scores, lengths, page_table, k: int, page_size: int):
         out[r, :len(pos)] = slots_from_positions(page_table[r:r + 1], pos[None, :].astype(np.int64),
                                                  page_size)[0].clip(min=-1)
     return out
+
+
+def union_groups_numpy(positions, page_table, group: int, page_size: int, out_cols: int):
+    """Union of the selections of token groups (the input of the grouped decode).
+
+    ``positions`` [tokens, k] (each token's selected positions, -1 = none); tokens
+    ``[g * group, (g + 1) * group)`` form group g with ``page_table`` row g. Per group: the
+    positions any token selected (0 <= pos < cols * page_size), ascending, as slot ids
+    through the group's table (-1 where the table has no page), with a membership byte
+    (bit j: token j of the group selected the position; 0 for a -1 slot); -1 / 0 after the
+    union up to ``out_cols``; and the union sizes. The grouped decode of token t equals
+    the decode of t's own selection (baseline.py:17-45), so the decode oracle for a group
+    is :func:`decode` per token. Pure numpy.
+    """
+    pos = np.asarray(positions, dtype=np.int64)
+    pt = np.asarray(page_table, dtype=np.int64)
+    tokens, _ = pos.shape
+    groups = tokens // group
+    max_pos = pt.shape[1] * page_size
+    slots = np.full((groups, out_cols), -1, dtype=np.int32)
+    member = np.zeros((groups, out_cols), dtype=np.uint8)
+    counts = np.zeros(groups, dtype=np.int32)
+    for g in range(groups):
+        bits = {}
+        for j in range(group):
+            for q in pos[g * group + j]:
+                if 0 <= q < max_pos:
+                    bits[int(q)] = bits.get(int(q), 0) | (1 << j)
+        u = np.array(sorted(bits), dtype=np.int64)
+        counts[g] = len(u)
+        u = u[:out_cols]
+        if len(u):
+            s = slots_from_positions(pt[g:g + 1], u[None, :], page_size)[0]
+            ok = s >= 0
+            slots[g, :len(u)] = np.where(ok, s, -1)
+            member[g, :len(u)] = np.where(ok, [bits[int(q)] for q in u], 0).astype(np.uint8)
+    return slots, member, counts
