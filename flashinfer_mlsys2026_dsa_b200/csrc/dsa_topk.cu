@@ -20,6 +20,12 @@
 // and an ordered compaction pass then write every position with key > T and the first
 // ones with key == T.  Each warp owns one contiguous segment of the row and reads it
 // coalesced, so positions come out in order without a sort.
+//
+// The first pass reads the row from global memory once, 16 bytes per load, and keeps the
+// keys in shared memory when every row of the call fits (up to kCapKeys positions), so the
+// other five passes read shared memory; otherwise every pass reads global memory.
+// The ordered compaction writes positions; a last pass translates them through the page
+// table, so that the page-table loads of a thread are in flight together.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +39,7 @@ namespace topk {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 256;  // one key byte per pass
+constexpr int kCapKeys = 48 * 1024;  // positions whose keys stay in shared memory (192 KB)
 
 struct Params {
   const float* scores;
@@ -108,7 +115,13 @@ __device__ __forceinline__ int select_bin(const uint32_t* hist, uint32_t need, u
   return *bin_out;
 }
 
+// kCached: the row's keys are kept in dynamic shared memory (every row of the call has at
+// most kCapKeys positions); otherwise each pass reads the scores from global memory.  Two
+// instances, because only the cached one raises the function's shared-memory limit (the
+// full carve-out leaves L1 too small for the uncached passes' re-reads).
+template <bool kCached>
 __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p) {
+  extern __shared__ uint32_t skey[];         // kCached: the row's keys
   __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
   __shared__ uint32_t hist[kBins];
   __shared__ uint32_t wsum[32];
@@ -129,6 +142,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     return;
   }
 
+  constexpr bool cached = kCached;
+  auto key_at = [&](int i) -> uint32_t {
+    if constexpr (kCached) return skey[i];
+    else return score_key(__ldg(sr + i));
+  };
+
   // ---- radix select of the k-th largest key, one key byte per pass (bits 31..24 first)
   uint32_t prefix = 0, need = (uint32_t)k;
   uint32_t* wh = whist[warp];
@@ -136,10 +155,32 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     const int sh = 24 - 8 * pass;
     for (int j = lane; j < kBins; j += 32) wh[j] = 0u;
     __syncwarp();
-    for (int i = threadIdx.x; i < L; i += kThreads) {
-      const uint32_t key = score_key(__ldg(sr + i));
-      // pass 0 takes every key; later passes the keys whose higher bytes equal the prefix
-      if (pass == 0 || (key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
+    if (pass == 0) {
+      // every key: 16-byte loads where the row is 16-byte aligned, keys kept if cached
+      const int nv = (reinterpret_cast<uintptr_t>(sr) & 15u) == 0 ? (L >> 2) : 0;
+      const float4* sr4 = reinterpret_cast<const float4*>(sr);
+#pragma unroll 2
+      for (int v = threadIdx.x; v < nv; v += kThreads) {
+        const float4 f = __ldg(sr4 + v);
+        const uint32_t k0 = score_key(f.x), k1 = score_key(f.y), k2 = score_key(f.z),
+                       k3 = score_key(f.w);
+        if constexpr (cached) reinterpret_cast<uint4*>(skey)[v] = make_uint4(k0, k1, k2, k3);
+        atomicAdd(&wh[k0 >> 24], 1u);
+        atomicAdd(&wh[k1 >> 24], 1u);
+        atomicAdd(&wh[k2 >> 24], 1u);
+        atomicAdd(&wh[k3 >> 24], 1u);
+      }
+      for (int i = 4 * nv + threadIdx.x; i < L; i += kThreads) {
+        const uint32_t key = score_key(__ldg(sr + i));
+        if constexpr (cached) skey[i] = key;
+        atomicAdd(&wh[key >> 24], 1u);
+      }
+    } else {
+      // the keys whose higher bytes equal the prefix
+      for (int i = threadIdx.x; i < L; i += kThreads) {
+        const uint32_t key = key_at(i);
+        if ((key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
+      }
     }
     __syncthreads();
     if (threadIdx.x < kBins) {
@@ -165,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   const int s0 = warp * seg, s1 = min(L, s0 + seg);
   uint32_t gt = 0, eq = 0;
   for (int i = s0 + lane; i < s1; i += 32) {
-    const uint32_t key = score_key(__ldg(sr + i));
+    const uint32_t key = key_at(i);
     gt += key > T;
     eq += key == T;
   }
@@ -189,15 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   uint32_t eq_seen = eq_before;
   for (int base = s0; base < s1; base += 32) {
     const int i = base + lane;
-    const uint32_t key = i < s1 ? score_key(__ldg(sr + i)) : 0u;
+    const uint32_t key = i < s1 ? key_at(i) : 0u;
     const bool is_eq = i < s1 && key == T;
     const uint32_t eq_mask = __ballot_sync(0xffffffffu, is_eq);
     const uint32_t eq_rank = eq_seen + __popc(eq_mask & ((1u << lane) - 1u));
     const bool take = i < s1 && (key > T || (is_eq && eq_rank < need));
     const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
-    if (take) out[pos_out + __popc(take_mask & ((1u << lane) - 1u))] = slot_of(p, pr, i);
+    if (take) out[pos_out + __popc(take_mask & ((1u << lane) - 1u))] = i;
     pos_out += __popc(take_mask);
     eq_seen += __popc(eq_mask);
+  }
+  // ---- positions to slot ids: a separate pass, so that the page-table loads of a thread's
+  // entries are in flight together instead of one per compaction step
+  if (pr != nullptr) {
+    __syncthreads();
+#pragma unroll 4
+    for (int j = threadIdx.x; j < k; j += kThreads) out[j] = slot_of(p, pr, out[j]);
   }
 }
 
@@ -331,8 +379,26 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
   p.k = k;
   p.slots = slots;
   p.slots_sb = slots_stride_b;
-  dsa::topk::topk_slots_kernel<<<(unsigned)num_rows, dsa::topk::kThreads, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(p);
+  // When every row fits (max_len <= kCapKeys) the keys stay in dynamic shared memory, a
+  // per-device function attribute of the cached instance, set once per device (not inside
+  // a stream capture when the first call ran eagerly).
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (max_len <= dsa::topk::kCapKeys) {
+    static std::atomic<bool> attr_set[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSA_ERR_CUDA;
+    if (!attr_set[dev].load(std::memory_order_acquire)) {
+      if (cudaFuncSetAttribute(dsa::topk::topk_slots_kernel<true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               dsa::topk::kCapKeys * 4) != cudaSuccess)
+        return DSA_ERR_CUDA;
+      attr_set[dev].store(true, std::memory_order_release);
+    }
+    dsa::topk::topk_slots_kernel<true><<<(unsigned)num_rows, dsa::topk::kThreads,
+                                         (size_t)max_len * 4, st>>>(p);
+  } else {
+    dsa::topk::topk_slots_kernel<false><<<(unsigned)num_rows, dsa::topk::kThreads, 0, st>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }
 
