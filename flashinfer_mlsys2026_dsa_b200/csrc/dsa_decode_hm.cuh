@@ -29,7 +29,7 @@ namespace dsa {
 namespace hm {
 
 constexpr int NH = 128;                   // heads of a row = the MMAs' M
-constexpr int kTS = 64;                   // slots per tile = the score MMA's N
+constexpr int kTS = 48;                   // slots per tile = the score MMA's N
 constexpr int kStages = 3;
 constexpr int kBlk = pipe::kBlk;
 constexpr int kProdWarps = pipe::kProdWarps;
@@ -51,7 +51,9 @@ constexpr int kXB = NH * kTS * 4;              // the peer's partial scores of a
 constexpr int OFF_KV = 0;
 constexpr int OFF_Q = kStages * kStageB;
 constexpr int OFF_X = OFF_Q + kQB;
-constexpr int OFF_BAR = OFF_X + kXB;
+constexpr int OFF_XS = OFF_X + kXB;            // this CTA's partials of a tile, staged for the
+                                               // bulk copy into the peer's X (same layout)
+constexpr int OFF_BAR = OFF_XS + kXB;
 constexpr int OFF_MASK = OFF_BAR + 512;        // [stage][kMaskStride] slot-validity words
 constexpr int OFF_MEMB = OFF_MASK + 128;       // grouped calls: [stage][kTS / 4] membership words
 constexpr int OFF_MISC = OFF_MEMB + 256;       // [0] TMEM base, [2] abort, [3] drain, [6] the
@@ -78,6 +80,8 @@ enum : int {
   B_PF = B_SE + 2, B_PD = B_PF + 2,       // [2] P written / PV done
   B_XF = B_PD + 2,                        // the peer's partial scores are in X (complete_tx)
   B_XE,                                   // the peer has read its X: we may write it again
+  B_XSF,                                  // the staging buffer holds a tile (4 sender warps)
+  B_XSE,                                  // the staging buffer's bulk copy has read it
   B_OF,                                   // the epilogue has read O
   B_PW,                                   // a split-K partial is written (8 warps)
   B_CNT,                                  // the merge's arrival count has been read
@@ -89,11 +93,11 @@ enum : int {
 static_assert(B_COUNT * 8 <= 512, "barrier block");
 __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * kProdWarps + blk; }
 
-// Byte offset of 16-byte chunk c (0..15) of head row h in an X buffer [128 heads][64 slots]
-// fp32; chunks are XOR-swizzled by the head so that a warp (32 heads, one chunk each) reads
+// Byte offset of 16-byte chunk c (0..11) of head row h in an X buffer [128 heads][48 slots]
+// fp32; chunks are rotated by h / 2 so that a warp (32 heads, one chunk each) reads or writes
 // with the minimum of four wavefronts.
 __device__ __forceinline__ uint32_t xoff(int h, int c) {
-  return (uint32_t)(h * (kTS * 4) + ((c ^ (h & 15)) << 4));
+  return (uint32_t)(h * (kTS * 4) + ((c + (h >> 1)) % (kTS / 4)) * 16);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -142,6 +146,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // st.async bytes landed; XE counts the peer's softmax warps, remotely.
     ptx::mbar_init(bar(B_XF), 1);
     ptx::mbar_init(bar(B_XE), kSoftmaxWarps);
+    ptx::mbar_init(bar(B_XSF), 4);
+    ptx::mbar_init(bar(B_XSE), 1);
     ptx::mbar_init(bar(B_OF), kSoftmaxWarps);
     ptx::mbar_init(bar(B_PW), kSoftmaxWarps);
     ptx::mbar_init(bar(B_CNT), 1);
@@ -219,7 +225,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           if (masks[st * kMaskStride + kMaskAny] != 0u) {  // an all-padding tile skips its MMAs
             ptx::tc_fence_after();
-            const uint32_t d_s = tmem + (uint32_t)(S_COL + kTS * sb);
+            const uint32_t d_s = tmem + (uint32_t)(S_COL + 64 * sb);
             const uint64_t ko = (uint64_t)((st * kStageB) >> 4);
 #pragma unroll
             for (int j = 0; j < kBlk; ++j)
@@ -297,9 +303,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ partial-score senders
     // Warps 8-11 (lane quadrant q = heads 32q .. 32q + 31): the tile's partial scores of
-    // this CTA, one head per thread (its 64 slots), streamed into the peer's X once the peer
-    // has read X for the previous tile.  The peer's softmax of that tile meanwhile goes on,
-    // so the exchange (bound by the cluster link) overlaps the softmax.
+    // this CTA, one head per thread (its 64 slots), staged in this CTA's shared memory in X's
+    // layout and sent into the peer's X with one bulk copy once the peer has read X for the
+    // previous tile.  The peer's softmax of that tile meanwhile goes on, so the exchange
+    // overlaps the softmax.
     ptx::regs_inc<kRegsHigh>();
     const int q = warp & 3;
     const int h = 32 * q + lane;
@@ -312,24 +319,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int sb = (int)(i & 1);
         ok = wait(bar(B_SF + sb), (uint32_t)((i >> 1) & 1));
         ptx::tc_fence_after();
-        uint32_t s0[32], s1[32];
-        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + kTS * sb), s0);
-        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + kTS * sb + 32), s1);
+        static_assert(kTS == 48, "the senders move 32 + 16 slots per head");
+        uint32_t s0[32], s1[16];
+        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + 64 * sb), s0);
+        ptx::tmem_ld16(tmem + lane_base + (uint32_t)(S_COL + 64 * sb + 32), s1);
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
         ok = __all_sync(0xffffffffu, ok);
         if (ok && lane == 0) ptx::mbar_arrive(bar(B_SE + sb));
-        // the peer has read its X for the previous tile: it may be written again
-        if (ok && i > 0) ok = __all_sync(0xffffffffu, wait(bar(B_XE), (uint32_t)((i - 1) & 1)));
+        // the staging buffer is free once the previous tile's bulk copy has read it
+        if (ok && i > 0) ok = __all_sync(0xffffffffu, wait(bar(B_XSE), (uint32_t)((i - 1) & 1)));
         if (!ok) break;
+        uint8_t* xs = sgen + OFF_XS;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          ptx::st_async_v4(x_peer + xoff(h, c), s0[4 * c], s0[4 * c + 1], s0[4 * c + 2],
-                           s0[4 * c + 3], xf_peer);
+          *reinterpret_cast<uint4*>(xs + xoff(h, c)) = make_uint4(s0[4 * c], s0[4 * c + 1], s0[4 * c + 2], s0[4 * c + 3]);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          ptx::st_async_v4(x_peer + xoff(h, 8 + c), s1[4 * c], s1[4 * c + 1], s1[4 * c + 2],
-                           s1[4 * c + 3], xf_peer);
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(xs + xoff(h, 8 + c)) = make_uint4(s1[4 * c], s1[4 * c + 1], s1[4 * c + 2], s1[4 * c + 3]);
+        ptx::fence_proxy_async_smem();  // the bulk copy (async proxy) reads these stores
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(B_XSF));
+        if (warp == kSm0) {
+          // One bulk copy of the tile's partials into the peer's X, once the four warps have
+          // staged theirs and the peer has read X for the previous tile; the staging buffer
+          // is released when the copy has read it.  (One copy instead of 4 x 32 x 16
+          // st.async: their per-instruction cost, not the link's bytes, set the tile period.)
+          bool go = true;
+          if (lane == 0) {
+            go = wait(bar(B_XSF), (uint32_t)(i & 1)) &&
+                 (i == 0 || wait(bar(B_XE), (uint32_t)((i - 1) & 1)));
+            if (go) {
+              ptx::bulk_s2peer(x_peer, sbase + (uint32_t)OFF_XS, (uint32_t)kXB, xf_peer);
+              ptx::bulk_commit_group();
+              ptx::bulk_wait_read_all();
+              ptx::mbar_arrive(bar(B_XSE));
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, (int)go, 0) != 0;
+        }
       }
     } else {
     // ------------------------------------------------------------------ softmax / epilogue
@@ -537,9 +565,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         bool ok = wait(bar(B_KVF + st), (uint32_t)((i / kStages) & 1)) &&
                   wait(bar(B_SF + sb), (uint32_t)((i >> 1) & 1));
         ptx::tc_fence_after();
-        uint32_t own0[32], own1[32];
-        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + kTS * sb), own0);
-        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + kTS * sb + 32), own1);
+        uint32_t own0[32], own1[16];
+        ptx::tmem_ld32(tmem + lane_base + (uint32_t)(S_COL + 64 * sb), own0);
+        ptx::tmem_ld16(tmem + lane_base + (uint32_t)(S_COL + 64 * sb + 32), own1);
         ptx::tmem_wait_ld();
         ptx::tc_fence_before();
         ok = __all_sync(0xffffffffu, ok);
@@ -552,11 +580,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         const uint32_t mw0 = masks[st * kMaskStride + 0], mw1 = masks[st * kMaskStride + 1];
         const bool live = masks[st * kMaskStride + kMaskAny] != 0u;
-        float x[64];
+        float x[kTS];
         float mt = -INFINITY;
         const int tok = kMember ? (h >> p.tok_shift) : 0;  // this head's token in the group
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < kTS / 4; ++c) {
           const float4 v = *reinterpret_cast<const float4*>(sgen + OFF_X + xoff(h, c));
           const float pv[4] = {v.x, v.y, v.z, v.w};
           const uint32_t mb = kMember ? memb[st * (kTS / 4) + c] >> tok : 0u;
@@ -618,15 +646,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         const float me = (m_run == -INFINITY) ? 0.f : m_run;
-        uint32_t pk[32];
+        uint32_t pk[16], pk2[8];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
+        for (int c = 0; c < kTS / 2; ++c) {
           const float a0 = ptx::ex2(x[2 * c] - me);
           const float a1 = ptx::ex2(x[2 * c + 1] - me);
           l_run += a0 + a1;
-          pk[c] = pack_bf16x2(a0, a1);
+          if (c < 16) pk[c] = pack_bf16x2(a0, a1);
+          else pk2[c - 16] = pack_bf16x2(a0, a1);
         }
-        ptx::tmem_st32(tmem + lane_base + (uint32_t)(P_COL + 32 * sb), pk);
+        ptx::tmem_st16(tmem + lane_base + (uint32_t)(P_COL + 32 * sb), pk);
+        ptx::tmem_st8(tmem + lane_base + (uint32_t)(P_COL + 32 * sb + 16), pk2);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();

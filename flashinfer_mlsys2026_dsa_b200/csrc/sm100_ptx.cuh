@@ -100,6 +100,24 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
+// Contiguous copy of `bytes` from this CTA's shared memory into another CTA's of the cluster
+// (dst and bar are shared::cluster addresses from mapa), completing `bytes` on bar there.
+__device__ __forceinline__ void bulk_s2peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "r"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// The bulk copies this thread issued so far form one group; wait until every such group has
+// finished reading its source (local shared memory: the wait ends once the copy has run,
+// whatever the destination CTA is doing).
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 // Global data written through the generic proxy (and acquired) becomes visible to this
 // thread's later async-proxy reads of global memory (bulk copies) after this fence.
 __device__ __forceinline__ void fence_proxy_async_global() {
