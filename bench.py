@@ -460,6 +460,11 @@ def run_ours(args):
     world, rank, local = _dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # The end-to-end leg's buffer-slot streams are the process's first streams, so that
+    # each gets a hardware queue of its own (created later, after the other legs' streams,
+    # two of them shared one in some runs and a step waited behind the previous slot).
+    NSLOT = 4
+    slot_stream = [torch.cuda.Stream(device=dev) for _ in range(NSLOT)]
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
@@ -526,42 +531,6 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         err |= read_device_errors(dev)
 
-    # ---------------- index production, the step before the decode: each row's top-k
-    # positions of index scores over its whole sequence, as slot ids, alone and chained
-    # with the decode (the ids cross HBM once, 8 KB per row)
-    index_rec = None
-    if not args.no_extra:
-        gsc = torch.Generator(device=dev).manual_seed(args.seed + 5)
-        topk_in = []
-        for w in sets:
-            sc = torch.randn(B, int(max(w.seq_lens)), generator=gsc, device=dev)
-            ln = torch.tensor(w.seq_lens, dtype=torch.int32, device=dev)
-            ids = torch.empty(B, w.topk, dtype=torch.int32, device=dev)
-            topk_in.append((sc, ln, ids, w))
-
-        def chained(a):
-            topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
-            kernel(a[3].q_nope, a[3].q_pe, a[3].ckv_cache, a[3].kpe_cache, a[2], a[3].sm_scale,
-                   out, lse)
-
-        warm = max(1, math.ceil(args.warmup / N_SETS))
-        t_ms = graph_ms([lambda a=a: topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
-                         for a in topk_in], reps, warm, stream, barrier)
-        c_ms = graph_ms([lambda a=a: chained(a) for a in topk_in], reps, warm, stream, barrier)
-        t_ms, c_ms = max_over_ranks([t_ms, c_ms], world, dev)
-        n_scores = sum(sum(a[3].seq_lens) for a in topk_in) / N_SETS
-        index_rec = {"topk_us_per_call": round(t_ms * 1e3, 2),
-                     "topk_then_decode_us_per_call": round(c_ms * 1e3, 2),
-                     "scores_per_call": int(n_scores),
-                     "scores_per_s": round(n_scores / (t_ms * 1e-3), 1),
-                     "method": "topk_slots(): fp32 index scores of every position of each row "
-                               "(seq_len 4k-32k) -> the 2048 best as slot ids, exact, one "
-                               "launch; then kernel() on those ids; CUDA-graph replay over "
-                               "the same 4 input sets as value"}
-        with torch.cuda.stream(stream):
-            err |= read_device_errors(dev)
-        del topk_in
-
     # ---------------- end to end through the public API, host buffers
     # Every step copies its query and index rows from pinned host memory, runs the public
     # kernel() and copies out/lse back.  Steps are pipelined the way a server runs them: a
@@ -588,7 +557,6 @@ def run_ours(args):
         for v, t in zip(views, (w.q_nope, w.q_pe, w.sparse_indices)):
             v.copy_(t.cpu())
         host_in.append(buf)
-    NSLOT = 4
     dev_in = [packed([sets[0].q_nope, sets[0].q_pe, sets[0].sparse_indices], device=dev)
               for _ in range(NSLOT)]
     out_proto = [torch.empty(B, H, 512, dtype=torch.bfloat16), torch.empty(B, H, dtype=torch.float32)]
@@ -596,7 +564,6 @@ def run_ours(args):
     host_out = [packed(out_proto, pinned=True) for _ in range(NSLOT)]
     h2d = host_in[0].numel()
     d2h = host_out[0][0].numel()
-    slot_stream = [torch.cuda.Stream(device=dev) for _ in range(NSLOT)]
     home = torch.cuda.current_stream(dev)
 
     assert NSLOT == N_SETS  # slot sl always carries input set sl
@@ -678,6 +645,42 @@ def run_ours(args):
         c1.record(slot_stream[0])
         c1.synchronize()
         copy_us[name] = c0.elapsed_time(c1) / steps * 1e3
+
+    # ---------------- index production, the step before the decode: each row's top-k
+    # positions of index scores over its whole sequence, as slot ids, alone and chained
+    # with the decode (the ids cross HBM once, 8 KB per row)
+    index_rec = None
+    if not args.no_extra:
+        gsc = torch.Generator(device=dev).manual_seed(args.seed + 5)
+        topk_in = []
+        for w in sets:
+            sc = torch.randn(B, int(max(w.seq_lens)), generator=gsc, device=dev)
+            ln = torch.tensor(w.seq_lens, dtype=torch.int32, device=dev)
+            ids = torch.empty(B, w.topk, dtype=torch.int32, device=dev)
+            topk_in.append((sc, ln, ids, w))
+
+        def chained(a):
+            topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
+            kernel(a[3].q_nope, a[3].q_pe, a[3].ckv_cache, a[3].kpe_cache, a[2], a[3].sm_scale,
+                   out, lse)
+
+        warm = max(1, math.ceil(args.warmup / N_SETS))
+        t_ms = graph_ms([lambda a=a: topk_slots(a[0], a[1], a[3].page_table, a[3].topk, out=a[2])
+                         for a in topk_in], reps, warm, stream, barrier)
+        c_ms = graph_ms([lambda a=a: chained(a) for a in topk_in], reps, warm, stream, barrier)
+        t_ms, c_ms = max_over_ranks([t_ms, c_ms], world, dev)
+        n_scores = sum(sum(a[3].seq_lens) for a in topk_in) / N_SETS
+        index_rec = {"topk_us_per_call": round(t_ms * 1e3, 2),
+                     "topk_then_decode_us_per_call": round(c_ms * 1e3, 2),
+                     "scores_per_call": int(n_scores),
+                     "scores_per_s": round(n_scores / (t_ms * 1e-3), 1),
+                     "method": "topk_slots(): fp32 index scores of every position of each row "
+                               "(seq_len 4k-32k) -> the 2048 best as slot ids, exact, one "
+                               "launch; then kernel() on those ids; CUDA-graph replay over "
+                               "the same 4 input sets as value"}
+        with torch.cuda.stream(stream):
+            err |= read_device_errors(dev)
+        del topk_in
 
     dev_ms, e2e_ms, paged_ms = max_over_ranks([dev_ms, e2e_ms, paged_ms], world, dev)
     ms_per_step = dev_ms / steps
