@@ -86,7 +86,7 @@ struct Cfg {
   static constexpr int kQB = kBlk * kQBlk + NH * 64;  // + the [NH x 32] SW64 q_pe block
   static constexpr int kPBlk = NH * 128;           // P^T: [NH x 64 slots] bf16 SW128 block
   static constexpr int kPB = 2 * kPBlk;            // P^T [NH x 128 slots], K-major
-  static constexpr int kXB = kTS * NH * 4;         // partial scores from the peer [kTS][NH]
+  static constexpr int kXB = kTS * NH * 4;         // partial scores from the peer (xo_t layout)
   static constexpr int OFF_Q = kStages * kStageB;
   static constexpr int OFF_P = OFF_Q + kQBufs * kQB;
   static constexpr int OFF_X = OFF_P + kPBufs * kPB;
@@ -129,6 +129,13 @@ enum : int {
   B_COUNT = B_DRAIN + 2
 };
 __host__ __device__ constexpr int kve(int stage, int blk) { return B_KVE + stage * kProdWarps + blk; }
+// Byte offset of the partial scores of slot `slot`, heads kHT*hh + c .. + 3 (c a multiple of
+// 4) in an exchange buffer X: [head half hh][head quad c / 4][slot] float4, so that the 32
+// slots of a warp write and read 512 contiguous bytes (four wavefronts per instruction).
+template <int kTS, int kHT>
+__device__ __forceinline__ uint32_t xo_t(int slot, int hh, int c) {
+  return (uint32_t)(((hh * (kHT / 4) + (c >> 2)) * kTS + slot) * 16);
+}
 // The exchange buffers X need no "empty" barrier.  A thread sends its partial of tile j
 // (into the peer's X[j % 2]) only after it finished tile j - 1, whose X wait needed every
 // peer thread's partial of tile j - 1; a peer thread sends that only after it finished
@@ -588,11 +595,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (__all_sync(0xffffffffu, ok) && lane == 0) ptx::mbar_arrive(bar(B_SE + sb));
         // st.async our partial into the peer's X[xb], completing its B_XF[xb] by bytes.
         if (ok && slot_ok) {
-          const uint32_t a = x_peer + (uint32_t)(xb * kXB + slot * (NH * 4) + hh * (kHT * 4));
+          const uint32_t a = x_peer + (uint32_t)(xb * kXB);
           const uint32_t xfb = xf_peer + 8u * (uint32_t)xb;
 #pragma unroll
           for (int c = 0; c < kHT; c += 4)
-            ptx::st_async_v4(a + 4u * (uint32_t)c, own[c], own[c + 1], own[c + 2], own[c + 3],
+            ptx::st_async_v4(a + xo_t<kTS, kHT>(slot, hh, c), own[c], own[c + 1], own[c + 2], own[c + 3],
                              xfb);
         }
         return ok;
@@ -619,7 +626,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (slot_ok)
                   v = *reinterpret_cast<const float4*>(
-                      sgen + OFF_X + xb * kXB + slot * (NH * 4) + hh * (kHT * 4) + 4 * c);
+                      sgen + OFF_X + xb * kXB + xo_t<kTS, kHT>(slot, hh, c));
                 pr[c] = v.x;
                 pr[c + 1] = v.y;
                 pr[c + 2] = v.z;
