@@ -146,6 +146,12 @@ static_assert(kStages * kMaskStride * 4 <= 128, "mask words");
 
 using pipe::desc;
 
+// Two bf16 (round to nearest), `lo` in the low half: two adjacent slots of one P^T row.
+__device__ __forceinline__ uint32_t pack_p2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // kPaged: sparse_indices holds token positions, translated through the page table by the
 // gather producers (ids are fetched two tiles ahead so the dependent page-table load is off
 // the producer's path).
@@ -703,14 +709,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!aborted) {  // else the next vote ends the loop for every thread
               uint8_t* pbuf = sgen + OFF_P + (int)(ip % kPBufs) * kPB + (slot >> 6) * C::kPBlk;
+              float pv[kHT];
 #pragma unroll
               for (int h = 0; h < kHT; ++h) {
                 const float me = (m_run[h] == -INFINITY) ? 0.f : m_run[h];
-                const float pv = ptx::ex2(x[h] - me);
-                l_part[h] += pv;
-                if (live && slot_ok)
-                  *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_off(kHT * hh + h, slot & 63)) =
-                      __float2bfloat16_rn(pv);
+                pv[h] = ptx::ex2(x[h] - me);
+                l_part[h] += pv[h];
+              }
+              // P^T rows are heads: a 4-byte word holds one head's two adjacent slots.  Per
+              // pair of heads (h, h + 1) a lane pair swaps one value, then the even lane writes
+              // head h's word and the odd lane head h + 1's (four stores instead of eight
+              // 2-byte stores that shared words)
+              const bool odd = (lane & 1) != 0;
+#pragma unroll
+              for (int h = 0; h < kHT; h += 2) {
+                const float r = __shfl_xor_sync(0xffffffffu, odd ? pv[h] : pv[h + 1], 1);
+                if (live && slot_ok) {
+                  const int hw = kHT * hh + h + (odd ? 1 : 0);
+                  const uint32_t w = odd ? pack_p2(r, pv[h + 1]) : pack_p2(pv[h], r);
+                  *reinterpret_cast<uint32_t*>(pbuf + sw128_off(hw, (slot & 63) & ~1)) = w;
+                }
               }
               ptx::fence_proxy_async_smem();
               ptx::tc_fence_before();
