@@ -13,7 +13,8 @@
 // Without a page table the output is the selected positions themselves (the input of the
 // token-group union below).
 //
-// One CTA per row (1024 threads).  Scores are mapped to order-preserving 32-bit keys; a
+// One CTA per row (1024 threads), or two (a cluster) when the call has at most half as many
+// rows as the GPU has SMs.  Scores are mapped to order-preserving 32-bit keys; a
 // radix select finds the k-th largest key T in four histogram passes over the key's bytes,
 // high to low (each later pass only over the keys that share the bytes already fixed), with
 // one 256-bin histogram per warp so that warps never contend for a counter; a counting pass
@@ -22,8 +23,8 @@
 // coalesced, so positions come out in order without a sort.
 //
 // The first pass reads the row from global memory once, 16 bytes per load, and keeps the
-// keys in shared memory when every row of the call fits (up to kCapKeys positions), so the
-// other five passes read shared memory; otherwise every pass reads global memory.
+// keys in shared memory when every row of the call fits (up to kCapKeys positions per CTA),
+// so the other five passes read shared memory; otherwise every pass reads global memory.
 // The ordered compaction writes positions; a last pass translates them through the page
 // table, so that the page-table loads of a thread are in flight together.
 #include <cuda_runtime.h>
@@ -40,6 +41,8 @@ constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBins = 256;  // one key byte per pass
 constexpr int kCapKeys = 48 * 1024;  // positions whose keys stay in shared memory (192 KB)
+// The same per CTA of a two-CTA row, whose static shared memory is 2 KB larger.
+constexpr int kCapKeysPart = 47 * 1024;
 
 struct Params {
   const float* scores;
@@ -115,20 +118,62 @@ __device__ __forceinline__ int select_bin(const uint32_t* hist, uint32_t need, u
   return *bin_out;
 }
 
-// kCached: the row's keys are kept in dynamic shared memory (every row of the call has at
-// most kCapKeys positions); otherwise each pass reads the scores from global memory.  Two
-// instances, because only the cached one raises the function's shared-memory limit (the
-// full carve-out leaves L1 too small for the uncached passes' re-reads).
-template <bool kCached>
+// ---- the two CTAs of a row (a cluster of two): every thread of both takes part
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Full cluster barrier: this CTA's earlier shared-memory writes are visible to the other
+// CTA, and the other CTA's to this one, once it returns.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+// Split form: the arrive says this thread's reads of the other CTA's shared memory are
+// complete; the wait (before exit) keeps the CTA, and so its shared memory, alive until the
+// other CTA has arrived too.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The 32-bit word at the same shared-memory address in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t ld_peer_u32(const uint32_t* local, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+  uint32_t ra, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+// kCached: the keys of a CTA's positions are kept in dynamic shared memory (every row of the
+// call fits); otherwise each pass reads the scores from global memory.  Two instances per
+// kParts, because only the cached one raises the function's shared-memory limit (the full
+// carve-out leaves L1 too small for the uncached passes' re-reads).
+//
+// kParts == 2: a row is split between the two CTAs of a cluster (used when the call has at
+// most half as many rows as the GPU has SMs, so that the other SMs are not left idle).  CTA
+// r holds the positions [lo_r, hi_r) (rank 0 the first half, rounded to 4 positions so that
+// both halves start 16-byte aligned); each pass adds the other CTA's histogram, read through
+// distributed shared memory after a cluster barrier, so that both CTAs pick the same bin and
+// end with the same T; rank 1's compaction then starts after rank 0's keys.  The output is
+// the same array as with one CTA per row.
+template <bool kCached, int kParts>
 __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p) {
-  extern __shared__ uint32_t skey[];         // kCached: the row's keys
+  static_assert(kParts == 1 || kParts == 2, "one or two CTAs per row");
+  extern __shared__ uint32_t skey[];         // kCached: the keys of this CTA's positions
   __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
-  __shared__ uint32_t hist[kBins];
+  __shared__ uint32_t hist[kBins];           // the row's histogram (both CTAs' added)
+  __shared__ uint32_t hpart[2][kBins];       // kParts == 2: this CTA's, pass p in [p & 1]
   __shared__ uint32_t wsum[32];
   __shared__ uint32_t above_s;
   __shared__ int bin_s;
   __shared__ uint32_t wcount[2][kWarps];  // per warp: keys > T, keys == T
-  const int row = blockIdx.x;
+  __shared__ uint32_t ccount[2];          // kParts == 2: this CTA's keys > T, keys == T
+  const int row = blockIdx.x / kParts;
+  const uint32_t part = kParts == 1 ? 0u : cta_rank_in_cluster();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* sr = p.scores + (int64_t)row * p.scores_sb;
   const int32_t* pr = p.pt ? p.pt + (int64_t)row * p.pt_sb : nullptr;
@@ -137,15 +182,22 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   L = L < 0 ? 0 : (L > p.max_len ? p.max_len : L);
   const int k = p.k;
 
-  if (L <= k) {  // every position, in order, then padding
-    for (int i = threadIdx.x; i < k; i += kThreads) out[i] = i < L ? slot_of(p, pr, i) : -1;
+  if (L <= k) {  // every position, in order, then padding (both CTAs return here together)
+    for (int i = (int)part * kThreads + threadIdx.x; i < k; i += kParts * kThreads)
+      out[i] = i < L ? slot_of(p, pr, i) : -1;
     return;
   }
 
+  // this CTA's positions [lo, hi)
+  const int half = kParts == 1 ? L : min(L, ((L >> 1) + 3) & ~3);
+  const int lo = part == 0 ? 0 : half, hi = part == 0 ? half : L;
+  const int n = hi - lo;
+  const float* sl = sr + lo;
+
   constexpr bool cached = kCached;
-  auto key_at = [&](int i) -> uint32_t {
-    if constexpr (kCached) return skey[i];
-    else return score_key(__ldg(sr + i));
+  auto key_at = [&](int j) -> uint32_t {  // j: index into [lo, hi)
+    if constexpr (kCached) return skey[j];
+    else return score_key(__ldg(sl + j));
   };
 
   // ---- radix select of the k-th largest key, one key byte per pass (bits 31..24 first)
@@ -157,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     __syncwarp();
     if (pass == 0) {
       // every key: 16-byte loads where the row is 16-byte aligned, keys kept if cached
-      const int nv = (reinterpret_cast<uintptr_t>(sr) & 15u) == 0 ? (L >> 2) : 0;
-      const float4* sr4 = reinterpret_cast<const float4*>(sr);
+      const int nv = (reinterpret_cast<uintptr_t>(sl) & 15u) == 0 ? (n >> 2) : 0;
+      const float4* sr4 = reinterpret_cast<const float4*>(sl);
 #pragma unroll 2
       for (int v = threadIdx.x; v < nv; v += kThreads) {
         const float4 f = __ldg(sr4 + v);
@@ -170,28 +222,36 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
         atomicAdd(&wh[k2 >> 24], 1u);
         atomicAdd(&wh[k3 >> 24], 1u);
       }
-      for (int i = 4 * nv + threadIdx.x; i < L; i += kThreads) {
-        const uint32_t key = score_key(__ldg(sr + i));
+      for (int i = 4 * nv + threadIdx.x; i < n; i += kThreads) {
+        const uint32_t key = score_key(__ldg(sl + i));
         if constexpr (cached) skey[i] = key;
         atomicAdd(&wh[key >> 24], 1u);
       }
     } else {
       // the keys whose higher bytes equal the prefix
-      for (int i = threadIdx.x; i < L; i += kThreads) {
+      for (int i = threadIdx.x; i < n; i += kThreads) {
         const uint32_t key = key_at(i);
         if ((key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
       }
     }
     __syncthreads();
+    uint32_t c = 0;
     if (threadIdx.x < kBins) {
-      uint32_t c = 0;
 #pragma unroll 8
       for (int w = 0; w < kWarps; ++w) c += whist[w][threadIdx.x];
-      hist[threadIdx.x] = c;
+      if constexpr (kParts == 1) hist[threadIdx.x] = c;
+      else hpart[pass & 1][threadIdx.x] = c;
     }
     if (threadIdx.x == 0) {
       bin_s = -1;
       above_s = 0u;
+    }
+    if constexpr (kParts == 2) {
+      // Both CTAs' histograms of this pass are complete.  hpart[pass & 1] is written again
+      // two passes later, after the next cluster barrier, which the other CTA reaches only
+      // once this read of it is done.
+      cluster_sync();
+      if (threadIdx.x < kBins) hist[threadIdx.x] = c + ld_peer_u32(&hpart[pass & 1][threadIdx.x], part ^ 1u);
     }
     __syncthreads();
     const int b = select_bin(hist, need, wsum, &above_s, &bin_s);
@@ -201,9 +261,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   }
   const uint32_t T = prefix;  // the k-th largest key; `need` keys equal to T are taken
 
-  // ---- counting pass: each warp owns a contiguous segment of the row
-  const int seg = (L + kWarps - 1) / kWarps;
-  const int s0 = warp * seg, s1 = min(L, s0 + seg);
+  // ---- counting pass: each warp owns a contiguous segment of this CTA's positions
+  const int seg = (n + kWarps - 1) / kWarps;
+  const int s0 = warp * seg, s1 = min(n, s0 + seg);
   uint32_t gt = 0, eq = 0;
   for (int i = s0 + lane; i < s1; i += 32) {
     const uint32_t key = key_at(i);
@@ -220,7 +280,26 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     wcount[1][warp] = eq;
   }
   __syncthreads();
-  uint32_t gt_before = 0, eq_before = 0;
+  // keys > T and == T at positions before this CTA's (rank 0's counts, for rank 1)
+  uint32_t gt_base = 0, eq_base = 0;
+  if constexpr (kParts == 2) {
+    if (threadIdx.x == 0) {
+      uint32_t g = 0, e = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        g += wcount[0][w];
+        e += wcount[1][w];
+      }
+      ccount[0] = g;
+      ccount[1] = e;
+    }
+    cluster_sync();
+    if (part == 1) {
+      gt_base = ld_peer_u32(&ccount[0], 0);
+      eq_base = ld_peer_u32(&ccount[1], 0);
+    }
+    cluster_arrive();  // no read of the other CTA's shared memory follows
+  }
+  uint32_t gt_before = gt_base, eq_before = eq_base;
   for (int w = 0; w < warp; ++w) {
     gt_before += wcount[0][w];
     eq_before += wcount[1][w];
@@ -236,17 +315,25 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     const uint32_t eq_rank = eq_seen + __popc(eq_mask & ((1u << lane) - 1u));
     const bool take = i < s1 && (key > T || (is_eq && eq_rank < need));
     const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
-    if (take) out[pos_out + __popc(take_mask & ((1u << lane) - 1u))] = i;
+    if (take) out[pos_out + __popc(take_mask & ((1u << lane) - 1u))] = lo + i;
     pos_out += __popc(take_mask);
     eq_seen += __popc(eq_mask);
   }
-  // ---- positions to slot ids: a separate pass, so that the page-table loads of a thread's
-  // entries are in flight together instead of one per compaction step
+  // ---- positions to slot ids: a separate pass over the entries this CTA wrote, so that
+  // the page-table loads of a thread's entries are in flight together instead of one per
+  // compaction step
   if (pr != nullptr) {
+    int j0 = 0, j1 = k;
+    if constexpr (kParts == 2) {
+      // rank 0 wrote [0, m0), rank 1 [m0, k), m0 = rank 0's keys > T and taken keys == T
+      const uint32_t m0 = part == 0 ? ccount[0] + min(ccount[1], need) : gt_base + min(eq_base, need);
+      (part == 0 ? j1 : j0) = (int)m0;
+    }
     __syncthreads();
 #pragma unroll 4
-    for (int j = threadIdx.x; j < k; j += kThreads) out[j] = slot_of(p, pr, out[j]);
+    for (int j = j0 + threadIdx.x; j < j1; j += kThreads) out[j] = slot_of(p, pr, out[j]);
   }
+  if constexpr (kParts == 2) cluster_wait();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -350,6 +437,25 @@ __global__ void __launch_bounds__(kThreads, 1) union_groups_kernel(const UnionPa
   if (threadIdx.x == 0 && p.counts) p.counts[g] = (int32_t)(n_out < INT32_MAX ? n_out : INT32_MAX);
 }
 
+// Launch with kParts CTAs per row (a cluster of that size).
+template <bool kCached, int kParts>
+int launch(const Params& p, int64_t rows, size_t smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(rows * kParts));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kParts;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kParts > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, topk_slots_kernel<kCached, kParts>, p) == cudaSuccess ? DSA_OK
+                                                                                         : DSA_ERR_CUDA;
+}
+
 }  // namespace topk
 }  // namespace dsa
 
@@ -379,27 +485,40 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
   p.k = k;
   p.slots = slots;
   p.slots_sb = slots_stride_b;
-  // When every row fits (max_len <= kCapKeys) the keys stay in dynamic shared memory, a
-  // per-device function attribute of the cached instance, set once per device (not inside
-  // a stream capture when the first call ran eagerly).
+  // Two CTAs per row (a cluster) when the call has at most half as many rows as the GPU has
+  // SMs.  When every row's keys fit (kCapKeys per CTA) they stay in dynamic shared memory,
+  // a per-device function attribute of the cached instances, set once per device (not
+  // inside a stream capture when the first call ran eagerly).
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (max_len <= dsa::topk::kCapKeys) {
-    static std::atomic<bool> attr_set[64];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSA_ERR_CUDA;
-    if (!attr_set[dev].load(std::memory_order_acquire)) {
-      if (cudaFuncSetAttribute(dsa::topk::topk_slots_kernel<true>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               dsa::topk::kCapKeys * 4) != cudaSuccess)
-        return DSA_ERR_CUDA;
-      attr_set[dev].store(true, std::memory_order_release);
-    }
-    dsa::topk::topk_slots_kernel<true><<<(unsigned)num_rows, dsa::topk::kThreads,
-                                         (size_t)max_len * 4, st>>>(p);
-  } else {
-    dsa::topk::topk_slots_kernel<false><<<(unsigned)num_rows, dsa::topk::kThreads, 0, st>>>(p);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSA_ERR_CUDA;
+  static std::atomic<int> sm_count[64];
+  static std::atomic<bool> attr_set[64];
+  int sms = sm_count[dev].load(std::memory_order_acquire);
+  if (sms == 0) {
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+      return DSA_ERR_CUDA;
+    sm_count[dev].store(sms, std::memory_order_release);
   }
-  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(dsa::topk::topk_slots_kernel<true, 1>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dsa::topk::kCapKeys * 4) != cudaSuccess ||
+        cudaFuncSetAttribute(dsa::topk::topk_slots_kernel<true, 2>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             dsa::topk::kCapKeysPart * 4) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    attr_set[dev].store(true, std::memory_order_release);
+  }
+  if (num_rows * 2 <= sms) {
+    const int per_cta = (max_len >> 1) + 4;  // the larger half of a row, rounded up
+    return per_cta <= dsa::topk::kCapKeysPart
+               ? dsa::topk::launch<true, 2>(p, num_rows, (size_t)per_cta * 4, st)
+               : dsa::topk::launch<false, 2>(p, num_rows, 0, st);
+  }
+  return max_len <= dsa::topk::kCapKeys
+             ? dsa::topk::launch<true, 1>(p, num_rows, (size_t)max_len * 4, st)
+             : dsa::topk::launch<false, 1>(p, num_rows, 0, st);
 }
 
 extern "C" int dsa_union_groups(const int32_t* positions, int64_t positions_stride_b,

@@ -48,6 +48,36 @@ def test_topk_slots_match_oracle(k, ties, special):
                                   oracle.topk_slots(sc, lengths, pt, k, 64))
 
 
+def _sm_count():
+    return torch.cuda.get_device_properties(0).multi_processor_count
+
+
+@pytest.mark.parametrize("max_len", [3000, 60000])
+def test_topk_slots_one_cta_per_row(max_len):
+    """More rows than half the SMs: one CTA per row (keys cached in shared memory at 3000
+    positions, read from global memory at 60000); the cases above have few rows and run
+    each row on a two-CTA cluster."""
+    rows = _sm_count() // 2 + 9
+    sc, lengths, pt = _case(21 + max_len, rows, max_len, ties=max_len == 3000)
+    np.testing.assert_array_equal(_run(sc, lengths, pt, 256, 64),
+                                  oracle.topk_slots(sc, lengths, pt, 256, 64))
+
+
+@pytest.mark.parametrize("ties", [False, True])
+def test_topk_slots_same_result_for_one_and_two_ctas_per_row(ties):
+    """The first rows of a call small enough for two CTAs per row, padded with copies of
+    them to a call that runs one CTA per row: the same slots."""
+    few = 16
+    sc, lengths, pt = _case(31 + ties, few, 20000, ties=ties)
+    lengths[2:6] = [20000, 19999, 2049, 4097]  # halves that are not multiples of 4
+    reps = (_sm_count() // 2) // few + 1
+    got_few = _run(sc, lengths, pt, 2048, 64)
+    got_many = _run(np.tile(sc, (reps, 1)), np.tile(lengths, reps), np.tile(pt, (reps, 1)), 2048, 64)
+    assert reps * few * 2 > _sm_count()
+    np.testing.assert_array_equal(got_few, got_many[:few])
+    np.testing.assert_array_equal(got_few, oracle.topk_slots(sc, lengths, pt, 2048, 64))
+
+
 def test_topk_slots_long_rows_and_token_granular_table():
     sc, lengths, pt = _case(11, 4, 131072)
     lengths[:] = [131072, 131071, 2049, 2048]
