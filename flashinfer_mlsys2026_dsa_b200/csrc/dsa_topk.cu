@@ -14,7 +14,7 @@
 // token-group union below).
 //
 // One CTA per row (1024 threads), or two (a cluster) when the call has at most half as many
-// rows as the GPU has SMs.  Scores are mapped to order-preserving 32-bit keys; a
+// rows as the GPU has SMs and long rows.  Scores are mapped to order-preserving 32-bit keys; a
 // radix select finds the k-th largest key T in four histogram passes over the key's bytes,
 // high to low (each later pass only over the keys that share the bytes already fixed), with
 // one 256-bin histogram per warp so that warps never contend for a counter; a counting pass
@@ -43,6 +43,10 @@ constexpr int kBins = 256;  // one key byte per pass
 constexpr int kCapKeys = 48 * 1024;  // positions whose keys stay in shared memory (192 KB)
 // The same per CTA of a two-CTA row, whose static shared memory is 2 KB larger.
 constexpr int kCapKeysPart = 47 * 1024;
+// Rows split between two CTAs only past this length: the split adds five cluster barriers
+// (about 2 us per call), which the halved passes repay on longer rows (measured on B200, 64
+// rows: 4k positions 11.3 us split against 9.2 whole, 32k positions 17.4 against 22.5).
+constexpr int kPartsMinLen = 12 * 1024;
 
 struct Params {
   const float* scores;
@@ -100,22 +104,54 @@ __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, uint32_t* w
   return r;
 }
 
-// Given the histogram `hist[kBins]` of the candidate keys' current byte and `need` (>= 1)
-// elements still to take from the top, the bin holding the need-th largest candidate, and
-// through *above how many candidates lie in higher bins.  Thread t < kBins owns bin
-// kBins - 1 - t (so the scan runs from the top bin down).
-__device__ __forceinline__ int select_bin(const uint32_t* hist, uint32_t need, uint32_t* wsum,
-                                          uint32_t* above, int* bin_out) {
-  const int b = kBins - 1 - (int)threadIdx.x;
-  const uint32_t mine = b >= 0 ? hist[b] : 0u;
-  const uint32_t incl = block_inclusive_scan(mine, wsum);  // candidates in bins >= b
-  const uint32_t excl = incl - mine;                       // candidates in bins > b
-  if (b >= 0 && excl < need && incl >= need) {
-    *bin_out = b;
-    *above = excl;
+// Given the histogram `hist[kBins]` of the candidate keys' current byte and `need` (>= 1,
+// at most the candidates' count) elements still to take from the top: the bin holding the
+// need-th largest candidate into *bin_out, and how many candidates lie in higher bins into
+// *above.  Run by one warp: lane l owns the eight bins 255 - 8l down to 248 - 8l, a warp scan
+// over the lanes' sums finds the lane, which walks its eight bins.
+__device__ __forceinline__ void select_bin_warp(const uint32_t* hist, uint32_t need,
+                                                uint32_t* above, int* bin_out) {
+  const int lane = threadIdx.x & 31;
+  const int top = kBins - 1 - 8 * lane;
+  uint32_t h[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    h[j] = hist[top - j];
+    sum += h[j];
   }
-  __syncthreads();
-  return *bin_out;
+  uint32_t incl = sum;  // candidates in bins >= top - 7
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  const uint32_t excl = incl - sum;  // candidates in bins > top
+  const bool mine = excl < need && incl >= need;
+  if (__ballot_sync(0xffffffffu, mine) == 0u) {  // need above the count: not reached
+    if (lane == 0) {
+      *bin_out = 0;
+      *above = 0u;
+    }
+    return;
+  }
+  if (mine) {
+    uint32_t acc = excl;
+    int b = top - 7;
+    bool done = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (!done) {
+        if (acc + h[j] >= need) {
+          b = top - j;
+          done = true;
+        } else {
+          acc += h[j];
+        }
+      }
+    }
+    *bin_out = b;
+    *above = acc;
+  }
 }
 
 // ---- the two CTAs of a row (a cluster of two): every thread of both takes part
@@ -154,7 +190,8 @@ __device__ __forceinline__ uint32_t ld_peer_u32(const uint32_t* local, uint32_t 
 // carve-out leaves L1 too small for the uncached passes' re-reads).
 //
 // kParts == 2: a row is split between the two CTAs of a cluster (used when the call has at
-// most half as many rows as the GPU has SMs, so that the other SMs are not left idle).  CTA
+// most half as many rows as the GPU has SMs, so that the other SMs are not left idle, and
+// rows longer than kPartsMinLen).  CTA
 // r holds the positions [lo_r, hi_r) (rank 0 the first half, rounded to 4 positions so that
 // both halves start 16-byte aligned); each pass adds the other CTA's histogram, read through
 // distributed shared memory after a cluster barrier, so that both CTAs pick the same bin and
@@ -167,7 +204,6 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
   __shared__ uint32_t hist[kBins];           // the row's histogram (both CTAs' added)
   __shared__ uint32_t hpart[2][kBins];       // kParts == 2: this CTA's, pass p in [p & 1]
-  __shared__ uint32_t wsum[32];
   __shared__ uint32_t above_s;
   __shared__ int bin_s;
   __shared__ uint32_t wcount[2][kWarps];  // per warp: keys > T, keys == T
@@ -242,10 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
       if constexpr (kParts == 1) hist[threadIdx.x] = c;
       else hpart[pass & 1][threadIdx.x] = c;
     }
-    if (threadIdx.x == 0) {
-      bin_s = -1;
-      above_s = 0u;
-    }
     if constexpr (kParts == 2) {
       // Both CTAs' histograms of this pass are complete.  hpart[pass & 1] is written again
       // two passes later, after the next cluster barrier, which the other CTA reaches only
@@ -253,11 +285,13 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
       cluster_sync();
       if (threadIdx.x < kBins) hist[threadIdx.x] = c + ld_peer_u32(&hpart[pass & 1][threadIdx.x], part ^ 1u);
     }
+    __syncthreads();  // hist complete
+    if (warp == 0) select_bin_warp(hist, need, &above_s, &bin_s);
+    // bin_s / above_s are written again only after two more barriers; the next pass's
+    // whist reset follows every read of whist (the sums above, before the last barrier)
     __syncthreads();
-    const int b = select_bin(hist, need, wsum, &above_s, &bin_s);
     need -= above_s;
-    prefix = (prefix << 8) | (uint32_t)b;
-    __syncthreads();
+    prefix = (prefix << 8) | (uint32_t)bin_s;
   }
   const uint32_t T = prefix;  // the k-th largest key; `need` keys equal to T are taken
 
@@ -486,9 +520,10 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
   p.slots = slots;
   p.slots_sb = slots_stride_b;
   // Two CTAs per row (a cluster) when the call has at most half as many rows as the GPU has
-  // SMs.  When every row's keys fit (kCapKeys per CTA) they stay in dynamic shared memory,
-  // a per-device function attribute of the cached instances, set once per device (not
-  // inside a stream capture when the first call ran eagerly).
+  // SMs and rows longer than kPartsMinLen.  When every row's keys fit (kCapKeys per CTA)
+  // they stay in dynamic shared memory, a per-device function attribute of the cached
+  // instances, set once per device (not inside a stream capture when the first call ran
+  // eagerly).
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSA_ERR_CUDA;
@@ -510,7 +545,7 @@ extern "C" int dsa_topk_slots(const float* scores, int64_t scores_stride_b, cons
       return DSA_ERR_CUDA;
     attr_set[dev].store(true, std::memory_order_release);
   }
-  if (num_rows * 2 <= sms) {
+  if (num_rows * 2 <= sms && max_len > dsa::topk::kPartsMinLen) {
     const int per_cta = (max_len >> 1) + 4;  // the larger half of a row, rounded up
     return per_cta <= dsa::topk::kCapKeysPart
                ? dsa::topk::launch<true, 2>(p, num_rows, (size_t)per_cta * 4, st)

@@ -40,10 +40,11 @@ def _case(seed, rows, max_len, ties=False, special=False, page_size=64):
     return sc, lengths, pt
 
 
+@pytest.mark.parametrize("max_len", [9000, 13000])  # one CTA per row; two (past 12k positions)
 @pytest.mark.parametrize("k", [1, 64, 2048])
 @pytest.mark.parametrize("ties,special", [(False, False), (True, False), (False, True)])
-def test_topk_slots_match_oracle(k, ties, special):
-    sc, lengths, pt = _case(k + 3 * ties + 5 * special, 12, 9000, ties, special)
+def test_topk_slots_match_oracle(k, ties, special, max_len):
+    sc, lengths, pt = _case(k + 3 * ties + 5 * special + max_len, 12, max_len, ties, special)
     np.testing.assert_array_equal(_run(sc, lengths, pt, k, 64),
                                   oracle.topk_slots(sc, lengths, pt, k, 64))
 
@@ -55,8 +56,7 @@ def _sm_count():
 @pytest.mark.parametrize("max_len", [3000, 60000])
 def test_topk_slots_one_cta_per_row(max_len):
     """More rows than half the SMs: one CTA per row (keys cached in shared memory at 3000
-    positions, read from global memory at 60000); the cases above have few rows and run
-    each row on a two-CTA cluster."""
+    positions, read from global memory at 60000)."""
     rows = _sm_count() // 2 + 9
     sc, lengths, pt = _case(21 + max_len, rows, max_len, ties=max_len == 3000)
     np.testing.assert_array_equal(_run(sc, lengths, pt, 256, 64),
@@ -65,8 +65,9 @@ def test_topk_slots_one_cta_per_row(max_len):
 
 @pytest.mark.parametrize("ties", [False, True])
 def test_topk_slots_same_result_for_one_and_two_ctas_per_row(ties):
-    """The first rows of a call small enough for two CTAs per row, padded with copies of
-    them to a call that runs one CTA per row: the same slots."""
+    """The first rows of a call small enough for two CTAs per row (rows past 12k
+    positions), padded with copies of them to a call that runs one CTA per row: the same
+    slots."""
     few = 16
     sc, lengths, pt = _case(31 + ties, few, 20000, ties=ties)
     lengths[2:6] = [20000, 19999, 2049, 4097]  # halves that are not multiples of 4
