@@ -107,50 +107,33 @@ __device__ __forceinline__ uint32_t block_inclusive_scan(uint32_t v, uint32_t* w
 // Given the histogram `hist[kBins]` of the candidate keys' current byte and `need` (>= 1,
 // at most the candidates' count) elements still to take from the top: the bin holding the
 // need-th largest candidate into *bin_out, and how many candidates lie in higher bins into
-// *above.  Run by one warp: lane l owns the eight bins 255 - 8l down to 248 - 8l, a warp scan
-// over the lanes' sums finds the lane, which walks its eight bins.
-__device__ __forceinline__ void select_bin_warp(const uint32_t* hist, uint32_t need,
-                                                uint32_t* above, int* bin_out) {
-  const int lane = threadIdx.x & 31;
-  const int top = kBins - 1 - 8 * lane;
-  uint32_t h[8], sum = 0;
+// *above.  Threads t < kBins (eight warps) own bin kBins - 1 - t: a warp scan over each
+// warp's 32 bins, the eight warp totals through `wtot` and one block barrier.  (One warp
+// walking eight bins per lane took ~1,800 cycles per pass, mostly its serial scan.)
+__device__ __forceinline__ void select_bin(const uint32_t* hist, uint32_t need, uint32_t* wtot,
+                                           uint32_t* above, int* bin_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kSelWarps = kBins / 32;
+  uint32_t incl = 0, mine = 0;
+  if (warp < kSelWarps) {
+    mine = hist[kBins - 1 - (int)threadIdx.x];
+    incl = mine;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    h[j] = hist[top - j];
-    sum += h[j];
-  }
-  uint32_t incl = sum;  // candidates in bins >= top - 7
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
-  }
-  const uint32_t excl = incl - sum;  // candidates in bins > top
-  const bool mine = excl < need && incl >= need;
-  if (__ballot_sync(0xffffffffu, mine) == 0u) {  // need above the count: not reached
-    if (lane == 0) {
-      *bin_out = 0;
-      *above = 0u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
     }
-    return;
+    if (lane == 31) wtot[warp] = incl;
   }
-  if (mine) {
-    uint32_t acc = excl;
-    int b = top - 7;
-    bool done = false;
+  __syncthreads();
+  if (warp < kSelWarps) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (!done) {
-        if (acc + h[j] >= need) {
-          b = top - j;
-          done = true;
-        } else {
-          acc += h[j];
-        }
-      }
+    for (int w = 0; w < kSelWarps; ++w) incl += w < warp ? wtot[w] : 0u;
+    const uint32_t excl = incl - mine;  // candidates in bins above this thread's
+    if (excl < need && incl >= need) {
+      *bin_out = kBins - 1 - (int)threadIdx.x;
+      *above = excl;
     }
-    *bin_out = b;
-    *above = acc;
   }
 }
 
@@ -204,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
   __shared__ uint32_t hist[kBins];           // the row's histogram (both CTAs' added)
   __shared__ uint32_t hpart[2][kBins];       // kParts == 2: this CTA's, pass p in [p & 1]
+  __shared__ uint32_t wtot[kBins / 32];      // bin selection: per-warp totals
   __shared__ uint32_t above_s;
   __shared__ int bin_s;
   __shared__ uint32_t wcount[2][kWarps];  // per warp: keys > T, keys == T
@@ -265,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
       }
     } else {
       // the keys whose higher bytes equal the prefix
+#pragma unroll 4
       for (int i = threadIdx.x; i < n; i += kThreads) {
         const uint32_t key = key_at(i);
         if ((key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
@@ -286,9 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
       if (threadIdx.x < kBins) hist[threadIdx.x] = c + ld_peer_u32(&hpart[pass & 1][threadIdx.x], part ^ 1u);
     }
     __syncthreads();  // hist complete
-    if (warp == 0) select_bin_warp(hist, need, &above_s, &bin_s);
-    // bin_s / above_s are written again only after two more barriers; the next pass's
-    // whist reset follows every read of whist (the sums above, before the last barrier)
+    select_bin(hist, need, wtot, &above_s, &bin_s);
+    // bin_s / above_s and wtot are written again only after two more barriers; the next
+    // pass's whist reset follows every read of whist (the sums above, before the last barrier)
     __syncthreads();
     need -= above_s;
     prefix = (prefix << 8) | (uint32_t)bin_s;
@@ -299,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   const int seg = (n + kWarps - 1) / kWarps;
   const int s0 = warp * seg, s1 = min(n, s0 + seg);
   uint32_t gt = 0, eq = 0;
+#pragma unroll 4
   for (int i = s0 + lane; i < s1; i += 32) {
     const uint32_t key = key_at(i);
     gt += key > T;
@@ -341,7 +327,26 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   // ---- ordered compaction: keys > T, and keys == T while fewer than `need` were taken
   uint32_t pos_out = gt_before + min(eq_before, need);
   uint32_t eq_seen = eq_before;
-  for (int base = s0; base < s1; base += 32) {
+  const uint32_t below = (1u << lane) - 1u;  // lanes before this one
+  constexpr int kU = 4;
+  int base = s0;
+  for (; base + 32 * kU <= s1; base += 32 * kU) {
+    uint32_t key[kU], em[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) key[u] = key_at(base + 32 * u + lane);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) em[u] = __ballot_sync(0xffffffffu, key[u] == T);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t eq_rank = eq_seen + __popc(em[u] & below);
+      const bool take = key[u] > T || (key[u] == T && eq_rank < need);
+      const uint32_t take_mask = __ballot_sync(0xffffffffu, take);
+      if (take) out[pos_out + __popc(take_mask & below)] = lo + base + 32 * u + lane;
+      pos_out += __popc(take_mask);
+      eq_seen += __popc(em[u]);
+    }
+  }
+  for (; base < s1; base += 32) {
     const int i = base + lane;
     const uint32_t key = i < s1 ? key_at(i) : 0u;
     const bool is_eq = i < s1 && key == T;
