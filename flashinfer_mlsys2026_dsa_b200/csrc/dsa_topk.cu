@@ -15,16 +15,17 @@
 //
 // One CTA per row (1024 threads), or two (a cluster) when the call has at most half as many
 // rows as the GPU has SMs and long rows.  Scores are mapped to order-preserving 32-bit keys; a
-// radix select finds the k-th largest key T in four histogram passes over the key's bytes,
-// high to low (each later pass only over the keys that share the bytes already fixed), with
-// one 256-bin histogram per warp so that warps never contend for a counter; a counting pass
+// radix select finds the k-th largest key T in three histogram passes, high bits first: the
+// top byte (one 256-bin histogram per warp, as score bytes crowd into few bins there), then
+// two 12-bit digits in one 4096-bin histogram per pass (each over the keys that share the
+// bits already fixed, which spread over the bins); a counting pass
 // and an ordered compaction pass then write every position with key > T and the first
 // ones with key == T.  Each warp owns one contiguous segment of the row and reads it
 // coalesced, so positions come out in order without a sort.
 //
 // The first pass reads the row from global memory once, 16 bytes per load, and keeps the
 // keys in shared memory when every row of the call fits (up to kCapKeys positions per CTA),
-// so the other five passes read shared memory; otherwise every pass reads global memory.
+// so the other four passes read shared memory; otherwise every pass reads global memory.
 // The ordered compaction writes positions; a last pass translates them through the page
 // table, so that the page-table loads of a thread are in flight together.
 #include <cuda_runtime.h>
@@ -39,13 +40,15 @@ namespace topk {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 256;  // one key byte per pass
+constexpr int kBins = 256;     // the first pass: the key's top byte
+constexpr int kBins12 = 4096;  // the second and third passes: 12 key bits each
 constexpr int kCapKeys = 48 * 1024;  // positions whose keys stay in shared memory (192 KB)
-// The same per CTA of a two-CTA row, whose static shared memory is 2 KB larger.
+// The same per CTA of a two-CTA row, whose static shared memory is 1 KB larger.
 constexpr int kCapKeysPart = 47 * 1024;
-// Rows split between two CTAs only past this length: the split adds five cluster barriers
-// (about 2 us per call), which the halved passes repay on longer rows (measured on B200, 64
-// rows: 4k positions 11.3 us split against 9.2 whole, 32k positions 17.4 against 22.5).
+// Rows split between two CTAs only past this length: the split adds a cluster barrier per
+// pass and one for the counts (about 0.5 us each), which the halved passes repay on longer
+// rows (measured on B200 with 64 rows, four-pass select: 4k positions 11.3 us split against
+// 9.2 whole, 32k positions 17.4 against 22.5).
 constexpr int kPartsMinLen = 12 * 1024;
 
 struct Params {
@@ -137,6 +140,51 @@ __device__ __forceinline__ void select_bin(const uint32_t* hist, uint32_t need, 
   }
 }
 
+// The same over kBins12 bins, from the four counts `cnt` of this thread's bins 4095 - 4t down
+// to 4092 - 4t (thread t of the block, highest first): a block scan of the per-thread sums
+// (warp shuffles, the 32 warp totals through `wtot32`, one block barrier), then the thread
+// whose range holds the need-th candidate walks its four bins.
+__device__ __forceinline__ void select_bin12(const uint32_t (&cnt)[4], uint32_t need,
+                                             uint32_t* wtot32, uint32_t* above, int* bin_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t mine = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+  uint32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) wtot32[warp] = incl;
+  __syncthreads();
+  uint32_t wt = wtot32[lane];  // inclusive scan of the warp totals, in every warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t n = __shfl_up_sync(0xffffffffu, wt, o);
+    if (lane >= o) wt += n;
+  }
+  const uint32_t before = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
+  incl += warp > 0 ? before : 0u;
+  const uint32_t excl = incl - mine;  // candidates in bins above this thread's four
+  if (excl < need && incl >= need) {
+    uint32_t acc = excl;
+    int b = kBins12 - 4 - 4 * (int)threadIdx.x;
+    bool done = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (!done) {
+        if (acc + cnt[j] >= need) {
+          b = kBins12 - 1 - 4 * (int)threadIdx.x - j;
+          done = true;
+        } else {
+          acc += cnt[j];
+        }
+      }
+    }
+    *bin_out = b;
+    *above = acc;
+  }
+}
+
 // ---- the two CTAs of a row (a cluster of two): every thread of both takes part
 __device__ __forceinline__ uint32_t cta_rank_in_cluster() {
   uint32_t r;
@@ -167,6 +215,19 @@ __device__ __forceinline__ uint32_t ld_peer_u32(const uint32_t* local, uint32_t 
   return v;
 }
 
+// The 16 bytes at the same (16-byte aligned) shared-memory address in CTA `rank`.
+__device__ __forceinline__ uint4 ld_peer_v4(const uint32_t* local, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+  uint32_t ra;
+  uint4 v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(ra)
+               : "memory");
+  return v;
+}
+
 // kCached: the keys of a CTA's positions are kept in dynamic shared memory (every row of the
 // call fits); otherwise each pass reads the scores from global memory.  Two instances per
 // kParts, because only the cached one raises the function's shared-memory limit (the full
@@ -184,10 +245,13 @@ template <bool kCached, int kParts>
 __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p) {
   static_assert(kParts == 1 || kParts == 2, "one or two CTAs per row");
   extern __shared__ uint32_t skey[];         // kCached: the keys of this CTA's positions
-  __shared__ uint32_t whist[kWarps][kBins];  // per-warp histograms of the current key byte
-  __shared__ uint32_t hist[kBins];           // the row's histogram (both CTAs' added)
-  __shared__ uint32_t hpart[2][kBins];       // kParts == 2: this CTA's, pass p in [p & 1]
-  __shared__ uint32_t wtot[kBins / 32];      // bin selection: per-warp totals
+  // the first pass's per-warp histograms of the top key byte; then (same memory) the
+  // 4096-bin histograms of the second and third passes, [pass - 1][bin]
+  __shared__ __align__(16) uint32_t whist[kWarps][kBins];
+  static_assert(kWarps * kBins == 2 * kBins12, "two 12-bit histograms in the first pass's memory");
+  __shared__ uint32_t hist[kBins];           // the first pass's row histogram (both CTAs' added)
+  __shared__ uint32_t hpart[kBins];          // kParts == 2: this CTA's first-pass histogram
+  __shared__ uint32_t wtot[kWarps];          // bin selection: per-warp totals
   __shared__ uint32_t above_s;
   __shared__ int bin_s;
   __shared__ uint32_t wcount[2][kWarps];  // per warp: keys > T, keys == T
@@ -220,40 +284,31 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     else return score_key(__ldg(sl + j));
   };
 
-  // ---- radix select of the k-th largest key, one key byte per pass (bits 31..24 first)
+  // ---- radix select of the k-th largest key: the top byte (bits 31..24), then bits 23..12,
+  // then bits 11..0, each later pass over the keys that share the bits already fixed
   uint32_t prefix = 0, need = (uint32_t)k;
-  uint32_t* wh = whist[warp];
-  for (int pass = 0; pass < 4; ++pass) {
-    const int sh = 24 - 8 * pass;
+  {
+    uint32_t* wh = whist[warp];
     for (int j = lane; j < kBins; j += 32) wh[j] = 0u;
     __syncwarp();
-    if (pass == 0) {
-      // every key: 16-byte loads where the row is 16-byte aligned, keys kept if cached
-      const int nv = (reinterpret_cast<uintptr_t>(sl) & 15u) == 0 ? (n >> 2) : 0;
-      const float4* sr4 = reinterpret_cast<const float4*>(sl);
+    // every key: 16-byte loads where the row is 16-byte aligned, keys kept if cached
+    const int nv = (reinterpret_cast<uintptr_t>(sl) & 15u) == 0 ? (n >> 2) : 0;
+    const float4* sr4 = reinterpret_cast<const float4*>(sl);
 #pragma unroll 2
-      for (int v = threadIdx.x; v < nv; v += kThreads) {
-        const float4 f = __ldg(sr4 + v);
-        const uint32_t k0 = score_key(f.x), k1 = score_key(f.y), k2 = score_key(f.z),
-                       k3 = score_key(f.w);
-        if constexpr (cached) reinterpret_cast<uint4*>(skey)[v] = make_uint4(k0, k1, k2, k3);
-        atomicAdd(&wh[k0 >> 24], 1u);
-        atomicAdd(&wh[k1 >> 24], 1u);
-        atomicAdd(&wh[k2 >> 24], 1u);
-        atomicAdd(&wh[k3 >> 24], 1u);
-      }
-      for (int i = 4 * nv + threadIdx.x; i < n; i += kThreads) {
-        const uint32_t key = score_key(__ldg(sl + i));
-        if constexpr (cached) skey[i] = key;
-        atomicAdd(&wh[key >> 24], 1u);
-      }
-    } else {
-      // the keys whose higher bytes equal the prefix
-#pragma unroll 4
-      for (int i = threadIdx.x; i < n; i += kThreads) {
-        const uint32_t key = key_at(i);
-        if ((key >> (sh + 8)) == prefix) atomicAdd(&wh[(key >> sh) & 0xFFu], 1u);
-      }
+    for (int v = threadIdx.x; v < nv; v += kThreads) {
+      const float4 f = __ldg(sr4 + v);
+      const uint32_t k0 = score_key(f.x), k1 = score_key(f.y), k2 = score_key(f.z),
+                     k3 = score_key(f.w);
+      if constexpr (cached) reinterpret_cast<uint4*>(skey)[v] = make_uint4(k0, k1, k2, k3);
+      atomicAdd(&wh[k0 >> 24], 1u);
+      atomicAdd(&wh[k1 >> 24], 1u);
+      atomicAdd(&wh[k2 >> 24], 1u);
+      atomicAdd(&wh[k3 >> 24], 1u);
+    }
+    for (int i = 4 * nv + threadIdx.x; i < n; i += kThreads) {
+      const uint32_t key = score_key(__ldg(sl + i));
+      if constexpr (cached) skey[i] = key;
+      atomicAdd(&wh[key >> 24], 1u);
     }
     __syncthreads();
     uint32_t c = 0;
@@ -261,22 +316,51 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
 #pragma unroll 8
       for (int w = 0; w < kWarps; ++w) c += whist[w][threadIdx.x];
       if constexpr (kParts == 1) hist[threadIdx.x] = c;
-      else hpart[pass & 1][threadIdx.x] = c;
+      else hpart[threadIdx.x] = c;
     }
     if constexpr (kParts == 2) {
-      // Both CTAs' histograms of this pass are complete.  hpart[pass & 1] is written again
-      // two passes later, after the next cluster barrier, which the other CTA reaches only
-      // once this read of it is done.
+      // both CTAs' first-pass histograms are complete; hpart is not written again
       cluster_sync();
-      if (threadIdx.x < kBins) hist[threadIdx.x] = c + ld_peer_u32(&hpart[pass & 1][threadIdx.x], part ^ 1u);
+      if (threadIdx.x < kBins) hist[threadIdx.x] = c + ld_peer_u32(&hpart[threadIdx.x], part ^ 1u);
     }
-    __syncthreads();  // hist complete
+    __syncthreads();  // hist complete; every read of whist is done
+    // the two 12-bit histograms (whist's memory) start at zero; the barrier below orders
+    // this before the second pass's counts
+    reinterpret_cast<uint4*>(&whist[0][0])[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(&whist[0][0])[threadIdx.x + kThreads] = make_uint4(0u, 0u, 0u, 0u);
     select_bin(hist, need, wtot, &above_s, &bin_s);
-    // bin_s / above_s and wtot are written again only after two more barriers; the next
-    // pass's whist reset follows every read of whist (the sums above, before the last barrier)
     __syncthreads();
     need -= above_s;
-    prefix = (prefix << 8) | (uint32_t)bin_s;
+    prefix = (uint32_t)bin_s;
+  }
+  for (int pass = 1; pass < 3; ++pass) {
+    uint32_t* h12 = &whist[0][0] + (pass - 1) * kBins12;
+    const int sh = pass == 1 ? 12 : 0;  // the pass's 12 bits are key bits [sh, sh + 12)
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+      const uint32_t key = key_at(i);
+      if ((key >> (sh + 12)) == prefix) atomicAdd(&h12[(key >> sh) & (kBins12 - 1)], 1u);
+    }
+    // this thread's bins 4095 - 4t .. 4092 - 4t, highest first (both CTAs' added); each
+    // 12-bit histogram is written in its pass only, so the other CTA may read it any time
+    // after the cluster barrier
+    const uint32_t* mine = h12 + (kBins12 - 4 - 4 * (int)threadIdx.x);
+    if constexpr (kParts == 2) cluster_sync();
+    else __syncthreads();
+    uint4 v = *reinterpret_cast<const uint4*>(mine);
+    if constexpr (kParts == 2) {
+      const uint4 r = ld_peer_v4(mine, part ^ 1u);
+      v.x += r.x;
+      v.y += r.y;
+      v.z += r.z;
+      v.w += r.w;
+    }
+    const uint32_t cnt[4] = {v.w, v.z, v.y, v.x};
+    select_bin12(cnt, need, wtot, &above_s, &bin_s);
+    // bin_s / above_s and wtot are written again only after two more barriers
+    __syncthreads();
+    need -= above_s;
+    prefix = (prefix << 12) | (uint32_t)bin_s;
   }
   const uint32_t T = prefix;  // the k-th largest key; `need` keys equal to T are taken
 
