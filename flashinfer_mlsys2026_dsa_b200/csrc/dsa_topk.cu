@@ -185,6 +185,15 @@ __device__ __forceinline__ void select_bin12(const uint32_t (&cnt)[4], uint32_t 
   }
 }
 
+// ---- programmatic dependent launch: the kernel is launched so that it may start while the
+// previous grid of the stream drains, and waits for that grid (griddepcontrol.wait) before
+// it reads global memory; once its threshold key is known it lets the next grid (the
+// decode) start its set-up, which itself waits for this grid before it reads the slot ids.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- the two CTAs of a row (a cluster of two): every thread of both takes part
 __device__ __forceinline__ uint32_t cta_rank_in_cluster() {
   uint32_t r;
@@ -256,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
   __shared__ int bin_s;
   __shared__ uint32_t wcount[2][kWarps];  // per warp: keys > T, keys == T
   __shared__ uint32_t ccount[2];          // kParts == 2: this CTA's keys > T, keys == T
+  wait_prior_grid();
   const int row = blockIdx.x / kParts;
   const uint32_t part = kParts == 1 ? 0u : cta_rank_in_cluster();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -363,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_slots_kernel(const Params p)
     prefix = (prefix << 12) | (uint32_t)bin_s;
   }
   const uint32_t T = prefix;  // the k-th largest key; `need` keys equal to T are taken
+  allow_next_grid();
 
   // ---- counting pass: each warp owns a contiguous segment of this CTA's positions
   const int seg = (n + kWarps - 1) / kWarps;
@@ -560,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) union_groups_kernel(const UnionPa
   if (threadIdx.x == 0 && p.counts) p.counts[g] = (int32_t)(n_out < INT32_MAX ? n_out : INT32_MAX);
 }
 
-// Launch with kParts CTAs per row (a cluster of that size).
+// Launch with kParts CTAs per row (a cluster of that size), as a programmatic dependent of
+// the stream's previous grid.
 template <bool kCached, int kParts>
 int launch(const Params& p, int64_t rows, size_t smem, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
@@ -568,13 +580,15 @@ int launch(const Params& p, int64_t rows, size_t smem, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kParts;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kParts;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = kParts > 1 ? 1 : 0;
+  cfg.numAttrs = kParts > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, topk_slots_kernel<kCached, kParts>, p) == cudaSuccess ? DSA_OK
                                                                                          : DSA_ERR_CUDA;
 }
