@@ -31,6 +31,8 @@ Reported numbers:
              aggregate us per global batch and HBM fraction (strong scaling).
   cpu_baseline  the CPU oracle (C restatement of solution/triton/baseline.py) on a
              bounded sample of the same workload, all host cores.
+  torch_gpu_restatement  (one GPU) the same decode math as unfused PyTorch ops on the GPU,
+             timed beside the kernel as a bar, with its difference from the kernel.
 
 With --impl reference the line reports the reference's CPU path instead (the oracle port;
 the reference itself is PyTorch code that cannot travel to the GPU host).
@@ -335,6 +337,71 @@ def workload_record(name, dev, stream, args, peaks, kernel, read_device_errors):
         rec["device_errors"] = read_device_errors(dev)
     del sets, calls, out, lse
     torch.cuda.empty_cache()
+    return rec
+
+
+def torch_restatement(w):
+    """The decode of solution/triton/baseline.py:17-45 as plain PyTorch ops on the tensors'
+    device: gather the selected rows of the flattened pools, fp32 logits over the 576-d key
+    scaled by sm_scale, -inf where the index is -1, base-2 log-sum-exp, softmax, PV, bf16
+    output.  An unfused GPU program of the same math, timed beside the kernel as a bar; it
+    is a restatement, not the reference's own code, whose sources are not on the GPU host."""
+    import torch
+
+    ckv = w.ckv_cache.reshape(-1, 512)
+    kpe = w.kpe_cache.reshape(-1, 64)
+    valid = w.sparse_indices != -1
+    safe = torch.where(valid, w.sparse_indices, torch.zeros_like(w.sparse_indices)).long()
+    kc = ckv[safe].float()  # [B, topk, 512]
+    kp = kpe[safe].float()  # [B, topk, 64]
+    logits = (torch.matmul(w.q_nope.float(), kc.transpose(1, 2)) +
+              torch.matmul(w.q_pe.float(), kp.transpose(1, 2))) * w.sm_scale
+    logits = logits.masked_fill(~valid[:, None, :], float("-inf"))
+    lse = torch.logsumexp(logits, dim=-1) * (1.0 / math.log(2.0))
+    out = torch.matmul(torch.softmax(logits, dim=-1), kc).to(torch.bfloat16)
+    return out, lse
+
+
+def torch_restatement_record(names, dev, stream, args, kernel):
+    """us per call of torch_restatement on each workload (one GPU, four rotating input sets,
+    eager calls timed with CUDA events on the launching stream), and its largest difference
+    from the kernel's output on the same inputs."""
+    import torch
+
+    from flashinfer_mlsys2026_dsa_b200 import workloads
+
+    rec = {}
+    for name in names:
+        sets = [workloads.make(name, device=dev, seed=args.seed * 97 + s) for s in range(N_SETS)]
+        B, H = sets[0].num_tokens, sets[0].num_heads
+        out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(B, H, dtype=torch.float32, device=dev)
+        reps = 3
+        with torch.cuda.stream(stream):
+            for w in sets:
+                torch_restatement(w)
+            stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                for w in sets:
+                    torch_restatement(w)
+            e1.record(stream)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) / (reps * len(sets)) * 1e3
+            ref_out, ref_lse = torch_restatement(sets[0])
+            kernel(*sets[0].args(), out, lse)
+            stream.synchronize()
+        ok = torch.isfinite(ref_lse)
+        rec[name] = {"us_per_call": round(us, 1),
+                     "max_abs_out_diff_vs_kernel": float((ref_out.float() - out.float()).abs().max()),
+                     "max_abs_lse_diff_vs_kernel": float((ref_lse[ok] - lse[ok]).abs().max())}
+        del sets, out, lse, ref_out, ref_lse
+        torch.cuda.empty_cache()
+    rec["method"] = ("the decode math of solution/triton/baseline.py:17-45 as unfused PyTorch ops "
+                     "on the GPU (gather, fp32 matmuls, masked softmax, base-2 LSE), eager, "
+                     "CUDA events; a restatement timed as a bar, not the reference's own code")
     return rec
 
 
@@ -710,9 +777,12 @@ def run_ours(args):
     b2048 = None if args.no_extra else b2048_record(dev, stream, args, peaks, kernel, world,
                                                     rank, barrier)
     multi = None
+    torch_bar = None
     if world == 1 and not args.no_extra:
         multi = multi_token_record(dev, stream, args, kernel, kernel_grouped, union_groups,
                                    read_device_errors)
+        torch_bar = torch_restatement_record(tuple(dict.fromkeys((args.workload, "b32_h128"))),
+                                             dev, stream, args, kernel)
 
     base = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -768,6 +838,8 @@ def run_ours(args):
         line["b2048"] = b2048
     if multi is not None:
         line["multi_token"] = multi
+    if torch_bar is not None:
+        line["torch_gpu_restatement"] = torch_bar
     if base is not None:
         line["cpu_baseline"] = base
     print(json.dumps(line), flush=True)
